@@ -1,0 +1,71 @@
+"""Extracts the reference's committed tiny-model goldens into tests/golden/tiny_g1.npz.
+
+Run once in a checkout that holds the reference (it is read-only input here):
+
+    python tests/golden/make_fixtures.py /path/to/reference
+
+Source: the reference's goldens/tiny/g1 set (README "The tiny set"): HF-named bf16 weights (model/model.safetensors),
+the pinned RoPE inverse frequencies and T_spec table (rope.safetensors), torch32 (fwd_f32.*) and torch64p (fwd_f64p.*)
+forward taps for prompts p0 (T=13) and p1 (T=1), logits for p2 (T=70) and the 64-step greedy ids and margins
+(greedy.safetensors). Nothing is recomputed: the arrays are copied as they are, bit for bit, so the tests can run
+where the reference is absent (the GPU box).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import struct
+import sys
+
+import numpy as np
+
+_DTYPES = {"F32": np.float32, "F64": np.float64, "I64": np.int64, "U32": np.uint32, "BF16": np.uint16,
+           "I32": np.int32, "U16": np.uint16}
+
+
+def read_safetensors(path: str) -> dict:
+    """Minimal safetensors reader (8-byte little-endian header length, JSON header, raw little-endian data).
+    BF16 tensors come back as their uint16 bit patterns."""
+    with open(path, "rb") as f:
+        raw = f.read()
+    (n,) = struct.unpack_from("<Q", raw, 0)
+    header = json.loads(raw[8:8 + n])
+    base = 8 + n
+    out = {}
+    for name, meta in header.items():
+        if name == "__metadata__":
+            continue
+        dt = _DTYPES[meta["dtype"]]
+        lo, hi = meta["data_offsets"]
+        out[name] = np.frombuffer(raw[base + lo:base + hi], dtype=dt).reshape(meta["shape"]).copy()
+    return out
+
+
+def main(reference_root: str) -> None:
+    g = os.path.join(reference_root, "goldens", "tiny", "g1")
+    arrays = {}
+    with open(os.path.join(g, "model", "config.json")) as f:
+        arrays["config_json"] = np.frombuffer(f.read().encode(), np.uint8)
+    with open(os.path.join(g, "manifest.json")) as f:
+        manifest = json.load(f)
+    for name, t in read_safetensors(os.path.join(g, "model", "model.safetensors")).items():
+        arrays["w/" + name] = t
+    rope = read_safetensors(os.path.join(g, "rope.safetensors"))
+    for k, v in rope.items():
+        arrays["rope/" + k] = v
+    for p in ("p0", "p1", "p2"):
+        for oracle, tag in (("fwd_f32", "torch32"), ("fwd_f64p", "torch64p")):
+            for k, v in read_safetensors(os.path.join(g, f"{oracle}.{p}.safetensors")).items():
+                arrays[f"{tag}/{p}/{k}"] = v
+    for k, v in read_safetensors(os.path.join(g, "greedy.safetensors")).items():
+        arrays["greedy/" + k] = v
+    for pr in manifest["prompts"]:
+        arrays["prompt/" + pr["name"]] = np.array(pr["ids"], np.int64)
+    out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tiny_g1.npz")
+    np.savez_compressed(out, **arrays)
+    print(f"wrote {out}: {len(arrays)} arrays, {os.path.getsize(out)} bytes")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
