@@ -1,0 +1,169 @@
+/*
+ * lrm_cuda.h -- the C ABI of liblrmcuda.so, the B200 (sm_100a) CUDA device for the LRM Qwen3 forward path.
+ *
+ * This is the native side of a new `Lrm.Gpu.Cuda` backend. It implements the reference's device/kernel contracts
+ * (src/Lrm.Gpu.Core/Backend.fs:104-161: IGpuBackendProvider, IGpuBackend, IGpuHeap, ICommandList, IKernelSet) with
+ * plain pointers, sizes and status codes, so a .NET host binds it with blittable P/Invoke (the idiom of
+ * src/Lrm.Gpu.D3D12.Interop/Native.fs:11-28) and a Python host with ctypes. No torch or CUDA type crosses the ABI.
+ *
+ * Rules that hold for every entry point:
+ *  - Every function returns an lrm_status; nothing throws across the ABI. LRM_ERR_CONTRACT is the reference's
+ *    GpuContractException (Dispatch.fs:149-234 rules, once-only rules); LRM_ERR_CUDA is a device or API failure,
+ *    the analogue of D3D12DeviceLostException (D3D12/Backend.fs:109). lrm_cuda_last_error gives the message.
+ *  - Calls on one device come from one thread at a time; devices are independent (docs/contracts/gpu-backend.md,
+ *    "Threading").
+ *  - Host pointers passed in are owned by the caller and only read or written during the call.
+ */
+#ifndef LRM_CUDA_H
+#define LRM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LRM_CUDA_ABI_VERSION 1
+
+typedef enum lrm_status {
+    LRM_OK = 0,
+    LRM_ERR_CONTRACT = 1,      /* a contract rule is broken (GpuContractException) */
+    LRM_ERR_CUDA = 2,          /* CUDA runtime/driver failure; the device may be lost */
+    LRM_ERR_TIMEOUT = 3,       /* a wait ran past its limit, or a kernel's bounded wait gave up */
+    LRM_ERR_ARGUMENT = 4,      /* a null handle/pointer or an impossible size */
+    LRM_ERR_OUT_OF_MEMORY = 5, /* device memory allocation failed */
+    LRM_ERR_STATE = 6,         /* call out of order: heap/table twice, list reused, ... */
+    LRM_ERR_NO_DEVICE = 7      /* no CUDA device with that index */
+} lrm_status;
+
+typedef struct lrm_device_s *lrm_device;   /* IGpuBackend (+ its IGpuHeap, created once) */
+typedef struct lrm_cmdlist_s *lrm_cmdlist; /* ICommandList */
+
+/* DeviceInfo (Backend.fs:9-27). */
+typedef struct lrm_device_info {
+    int32_t index;
+    char name[256];         /* marketing name, e.g. "NVIDIA B200" */
+    uint32_t vendor_id;     /* PCI vendor id, 0x10de */
+    uint32_t pci_device_id; /* PCI device id from sysfs (0 when unreadable) */
+    char driver[64];        /* kernel driver version, e.g. "580.159" */
+    int64_t memory_bytes;
+    int32_t sm_count;
+    int32_t cc_major, cc_minor;
+    int32_t accepted;       /* 1 when the device meets the requirements (sm_100 family) */
+    char rejection[256];    /* why not, when accepted == 0 */
+} lrm_device_info;
+
+/* DeviceOptions flags (Backend.fs:30-55). */
+#define LRM_CUDA_DEBUG 0x1u            /* synchronise and check after every dispatch */
+#define LRM_CUDA_TIME_DISPATCHES 0x2u  /* time every dispatch; results follow the timers as gpu.dispatch */
+
+/* Completion (Backend.fs:84-92). */
+typedef struct lrm_completion {
+    uint64_t fence;
+    uint32_t dispatches;
+    uint32_t timer_count; /* user timers in opening order, then one per dispatch with TIME_DISPATCHES */
+} lrm_completion;
+
+/* ---- library ------------------------------------------------------------------------------------------------ */
+
+/* LRM_CUDA_ABI_VERSION of the loaded library. */
+int32_t lrm_cuda_abi_version(void);
+
+/* Copies the last error message of `dev` (or of the calling thread when dev is NULL) into buf; returns its length. */
+size_t lrm_cuda_last_error(lrm_device dev, char *buf, size_t n);
+
+/* ---- IGpuBackendProvider (Backend.fs:154-161) ---------------------------------------------------------------- */
+
+/* Number of CUDA devices (Enumerate). */
+lrm_status lrm_cuda_device_count(int32_t *count);
+
+/* DeviceCandidate for one index: info plus accepted/rejection (Backend.fs:21-27). */
+lrm_status lrm_cuda_device_info(int32_t index, lrm_device_info *out);
+
+/* Create: a backend on device `index` with LRM_CUDA_* flags. */
+lrm_status lrm_cuda_create(int32_t index, uint32_t flags, lrm_device *out);
+
+/* Dispose: waits for outstanding work and frees every page, list and event. */
+lrm_status lrm_cuda_destroy(lrm_device dev);
+
+/* ---- IGpuBackend ---------------------------------------------------------------------------------------------- */
+
+/* CreateHeap (Backend.fs:141, gpu-backend.md "IGpuBackend"): allocates the table (slot 0, 1 MiB) and pages 1..n of a
+ * HeapLayout; arenas[i] is the ArenaKind code of page i+1. Exactly once. */
+lrm_status lrm_cuda_create_heap(lrm_device dev, int32_t page_count, const uint32_t *arenas, const uint64_t *bytes);
+
+/* LoadKernels (Backend.fs:143): the catalog kernels are compiled into the library for sm_100a; this marks them loaded
+ * (exactly once) and returns the SHA-256 of the library's kernel set, the CUDA counterpart of ShaderSetHash. */
+lrm_status lrm_cuda_load_kernels(lrm_device dev, uint8_t set_hash[32]);
+
+/* IKernelSet.Contains (Backend.fs:96-100). */
+lrm_status lrm_cuda_kernel_present(lrm_device dev, uint32_t kernel_id, int32_t *present);
+
+/* Begin (Backend.fs:145): a new, empty command list. */
+lrm_status lrm_cuda_begin(lrm_device dev, lrm_cmdlist *out);
+
+/* Submit (Backend.fs:147): closes the list and enqueues it on the device's stream; *fence = 1, 2, 3, ... A list is
+ * submitted once. The list handle stays valid (closed) until lrm_cuda_list_free or lrm_cuda_destroy. */
+lrm_status lrm_cuda_submit(lrm_cmdlist list, uint64_t *fence);
+
+/* Frees a command list handle (closed or not). */
+lrm_status lrm_cuda_list_free(lrm_cmdlist list);
+
+/* Wait (Backend.fs:149): blocks until `fence` completed or `timeout_ms` passed (LRM_ERR_TIMEOUT, the device stays
+ * usable). Waiting again returns the same completion. */
+lrm_status lrm_cuda_wait(lrm_device dev, uint64_t fence, uint32_t timeout_ms, lrm_completion *out);
+
+/* One TimerResult of a completed submission (Backend.fs:70-79): the timer id (or 0x80000000 | kernel id for a
+ * gpu.dispatch timing), start in ns from the device's creation, duration in ns. */
+lrm_status lrm_cuda_timer_result(lrm_device dev, uint64_t fence, uint32_t index, uint32_t *timer_id,
+                                 int64_t *start_ns, int64_t *duration_ns);
+
+/* The fp32 denormal probe (Backend.fs:455-531, Fp32Denormals): runs scale_f32 with a = 0.5 over the 7 probe input
+ * words on a private buffer and returns the 7 result words for the host to classify (preserve / flush / mixed). */
+lrm_status lrm_cuda_denormal_probe(lrm_device dev, const uint32_t inputs[7], uint32_t results[7]);
+
+/* ---- IGpuHeap (Backend.fs:102-116) ---------------------------------------------------------------------------- */
+
+/* WriteTable: the sealed 1 MiB table image into slot 0, exactly once, before the first dispatch. */
+lrm_status lrm_cuda_write_table(lrm_device dev, const void *image, uint64_t bytes);
+
+/* Upload: host bytes into a page (slot 1..63); offset and size multiples of 4, inside the page. Waits for all
+ * submitted work first and returns when the copy is done. UploadFrom is this call on chunks of at most 64 MiB. */
+lrm_status lrm_cuda_upload(lrm_device dev, int32_t slot, uint64_t offset, const void *src, uint64_t bytes);
+
+/* Download: page (or table, slot 0) bytes to the host; waits for all submitted work first. */
+lrm_status lrm_cuda_download(lrm_device dev, int32_t slot, uint64_t offset, void *dst, uint64_t bytes);
+
+/* ---- ICommandList (Backend.fs:118-134) ------------------------------------------------------------------------ */
+
+/* Dispatch: records one catalog kernel with its 32-word argument block as Dispatch.prepare returned it (word 0 =
+ * the physical groups in x). The library re-checks the block against the sealed table: kernel id, word rules, token
+ * rows, dtypes, read-only and contiguity, aliasing, the catalog grid, and every minimum element count of
+ * docs/contracts/kernel-abi.md, so a bad block is refused before any launch. */
+lrm_status lrm_cuda_dispatch(lrm_cmdlist list, uint32_t kernel_id, const uint32_t words[32]);
+
+/* Barrier: every earlier command's writes are visible to every later command. */
+lrm_status lrm_cuda_barrier(lrm_cmdlist list);
+
+/* Copy: bytes between pages (slots 1..63), equal positive sizes, multiples of 4, no overlap; a full barrier. */
+lrm_status lrm_cuda_copy(lrm_cmdlist list, int32_t src_slot, uint64_t src_offset, int32_t dst_slot,
+                         uint64_t dst_offset, uint64_t bytes);
+
+/* BeginTimer / EndTimer: GPU-timed regions; timers nest and close in reverse order. */
+lrm_status lrm_cuda_timer_begin(lrm_cmdlist list, uint32_t *timer_id);
+lrm_status lrm_cuda_timer_end(lrm_cmdlist list, uint32_t timer_id);
+
+/* ---- host helpers ------------------------------------------------------------------------------------------- */
+
+/* T_spec (src/Lrm.Tensor.CpuReference/Rope.fs:163-251): cos/sin [max_pos, half] float32 with
+ * freq = f32(f32(pos) * inv_freq[j]) and the correctly rounded float64 cos/sin rounded to float32. Every rounding is
+ * certified; LRM_ERR_ARGUMENT when one cannot be (never seen for the tiny and Qwen3 tables). Needs no GPU. */
+lrm_status lrm_rope_table(const uint32_t *inv_freq_bits, int32_t half, int32_t max_pos, float *cos_out,
+                          float *sin_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LRM_CUDA_H */

@@ -1,0 +1,70 @@
+"""liblrmcuda.so without a GPU: it loads, exports every function include/*.h declares, and its host-only helpers
+(the certified T_spec builder) match the reference's pinned digests. No kernel is launched here."""
+
+import hashlib
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from rosylnalive_b200 import native as N
+from rosylnalive_b200 import rope as R
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for f in os.listdir(inc):
+        if not f.endswith(".h"):
+            continue
+        text = open(os.path.join(inc, f)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*(?:lrm_status|int32_t|size_t|void|uint32_t|int)\s+\*?\s*(lrm_\w+)\s*\(", text,
+                             flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for required in ("lrm_cuda_create", "lrm_cuda_create_heap", "lrm_cuda_write_table", "lrm_cuda_upload",
+                     "lrm_cuda_download", "lrm_cuda_begin", "lrm_cuda_dispatch", "lrm_cuda_barrier", "lrm_cuda_copy",
+                     "lrm_cuda_timer_begin", "lrm_cuda_timer_end", "lrm_cuda_submit", "lrm_cuda_wait",
+                     "lrm_cuda_last_error", "lrm_cuda_destroy"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", N.LIB_PATH], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = declared_functions() - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+
+
+def test_library_loads_and_reports_abi():
+    assert N.lib().lrm_cuda_abi_version() == 1
+    for name in N.SIGNATURES:
+        assert hasattr(N.lib(), name)
+
+
+def test_product_t_spec_equals_pinned_tables(tiny_golden):
+    cos, sin = N.rope_table(tiny_golden["rope/inv_freq.bits"], 512)
+    assert np.array_equal(cos.view(np.uint32), tiny_golden["rope/t_spec.cos"].view(np.uint32))
+    assert np.array_equal(sin.view(np.uint32), tiny_golden["rope/t_spec.sin"].view(np.uint32))
+    cos, sin = N.rope_table(R.QWEN3_INV_FREQ_BITS, 8192)
+    assert hashlib.sha256(cos.tobytes() + sin.tobytes()).hexdigest() == \
+        "da820d286cb666557f4cae3fa7f806c07d941653769e10c09021555a8f6ebfaf"
+
+
+def test_torch_inv_freq_matches_pins(tiny_golden):
+    assert np.array_equal(R.torch_inv_freq_bits(1e6, 128), R.QWEN3_INV_FREQ_BITS)
+    assert np.array_equal(R.torch_inv_freq_bits(1e6, 32), tiny_golden["rope/inv_freq.bits"])
+
+
+def test_rope_table_rejects_bad_arguments():
+    with pytest.raises(ValueError):
+        N.rope_table(np.array([0x7F800000], np.uint32), 4)  # inf
