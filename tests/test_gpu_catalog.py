@@ -26,8 +26,8 @@ POISON = 0x7FBADBAD
 
 
 def rel_l2(a, ref):
-    a = np.asarray(a, np.float64)
-    ref = np.asarray(ref, np.float64)
+    a = np.asarray(a, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
     return float(np.linalg.norm(a - ref) / max(np.linalg.norm(ref), 1e-300))
 
 
