@@ -154,6 +154,43 @@ lrm_status lrm_cuda_copy(lrm_cmdlist list, int32_t src_slot, uint64_t src_offset
 lrm_status lrm_cuda_timer_begin(lrm_cmdlist list, uint32_t *timer_id);
 lrm_status lrm_cuda_timer_end(lrm_cmdlist list, uint32_t timer_id);
 
+/* ---- fast-path operators on device memory ------------------------------------------------------------------- */
+/*
+ * The bf16 forward path's operators, for callers that manage device memory themselves (the Qwen engine below, the
+ * tests). Pointers are device addresses as uint64; `stream` is a cudaStream_t (NULL = the legacy default stream).
+ * Each call checks its arguments (alignment, sizes) and launches asynchronously; a kernel whose bounded wait gave up
+ * writes a nonzero code into the current device's error word (lrm_op_error_word).
+ */
+
+/* Makes `device` current for the calling thread and initialises its operator state. */
+lrm_status lrm_op_set_device(int32_t device);
+
+/* Reads the current device's error word (0 = no kernel reported a timeout); clears it when `clear` != 0. */
+lrm_status lrm_op_error_word(uint32_t *code, int32_t clear);
+
+#define LRM_GEMM_F32 0     /* out_f32[m, n] = acc */
+#define LRM_GEMM_RESID 1   /* out_f32[m, n] = resid[m, n] + acc (resid may equal out) */
+#define LRM_GEMM_SWIGLU 2  /* b rows interleave gate/up in blocks of 64; out_bf16[m, n/2] = silu(gate) * up */
+#define LRM_GEMM_PARTIAL 3 /* split-K partials, transposed: out_f32[split][n][m] */
+#define LRM_GEMM_BF16 4    /* out_bf16[m, n] = acc */
+
+/* D = A * B^T with A bf16 [m, k] and B bf16 [n, k] (both K-major) on tcgen05 tensor cores, fp32 accumulation in
+ * TMEM, TMA-fed; replaces the reference's matmul_bf16w (src/Lrm.Shaders/hlsl/kernels/matmul/matmul_bf16w.hlsl) on the
+ * bf16 path, with its epilogue fusions. */
+typedef struct lrm_gemm_desc {
+    int32_t m, n, k;
+    uint64_t a, b;
+    int32_t epilogue; /* LRM_GEMM_* */
+    int32_t bn;       /* output tile width 64, 128 or 256; 0 chooses */
+    int32_t splits;   /* split-K count; > 1 only with LRM_GEMM_PARTIAL */
+    uint64_t out;     /* fp32, bf16 or partial output */
+    int32_t ldo;      /* output leading dimension (elements); for PARTIAL the token stride, normally m */
+    uint64_t resid;   /* RESID: fp32 [m, ldr] */
+    int32_t ldr;
+    uint64_t split_stride; /* PARTIAL: elements between split slices */
+} lrm_gemm_desc;
+lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *desc);
+
 /* ---- host helpers ------------------------------------------------------------------------------------------- */
 
 /* T_spec (src/Lrm.Tensor.CpuReference/Rope.fs:163-251): cos/sin [max_pos, half] float32 with

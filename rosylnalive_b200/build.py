@@ -25,6 +25,8 @@ SOURCES = [
     "device.cu",
     "catalog_kernels.cu",
     "rope_host.cpp",
+    "ops.cu",
+    "gemm_tcgen05.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -1,0 +1,36 @@
+// gemm.h -- the tcgen05 GEMM's arguments (internal).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace lrm {
+
+enum GemmEpi : int { EPI_F32 = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_BF16 = 4 };
+
+struct GemmArgs {
+    int M, N, K;
+    const void *A;  // bf16 [M, K]
+    const void *B;  // bf16 [N, K]
+    int epi;
+    int bn;            // 64, 128 or 256
+    int splits;        // split-K count (EPI_PARTIAL only)
+    int kb_per_split;  // 64-wide k blocks per split
+    float *out_f32;
+    __nv_bfloat16 *out_bf16;
+    int ldo;  // leading dimension of the output (elements); for EPI_PARTIAL the token stride (= M)
+    const float *resid;
+    int ldr;
+    float *partial;
+    size_t split_stride;  // elements between split slices of `partial`
+    uint32_t *err;        // device error word: bounded waits write a code here
+};
+
+// nullptr when the arguments are valid, else the reason.
+const char *gemm_check(const GemmArgs &a);
+// Encodes the tensor maps and launches the persistent kernel on `sms` CTAs at most.
+cudaError_t gemm_launch(const GemmArgs &a, int sms, cudaStream_t stream);
+
+}  // namespace lrm

@@ -1,0 +1,378 @@
+// gemm_tcgen05.cu -- D = A * B^T on the 5th-generation tensor cores (tcgen05) for sm_100a.
+//
+// A [M, K] and B [N, K] are bf16, K-major (the PyTorch Linear layout for weights; activations row-major); the
+// accumulation is fp32 in tensor memory (TMEM). One persistent CTA per SM walks the output tiles (128 x BN) and, with
+// split-K, the K ranges:
+//   warp 0      TMA producer: one elected thread loads A and B k-blocks (64 wide, 128-byte swizzle) into a ring of
+//               STAGES shared-memory stages, each completing a `full` mbarrier;
+//   warp 1      allocates TMEM (2 x BN columns: two accumulators, so the epilogue of tile i overlaps the MMAs of tile
+//               i + 1) and one elected thread issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide k step, releasing a
+//               stage with tcgen05.commit on its `empty` mbarrier and a finished accumulator on `acc_full`;
+//   warps 2..5  epilogue: each thread owns one accumulator row (TMEM lane), reads it 16 columns at a time with
+//               tcgen05.ld and applies the epilogue, then frees the accumulator on `acc_empty`.
+// No TMA multicast is used. Every mbarrier wait is bounded (ptx::mbar_wait) and reports a code in the error word.
+//
+// Epilogues:
+//   EPI_F32      out_f32[m, n] = acc
+//   EPI_RESID    out_f32[m, n] = resid[m, n] + acc      (resid may be out: the residual stream updated in place)
+//   EPI_SWIGLU   B rows are gate/up interleaved in blocks of 64 (gate 64, up 64, ...); out_bf16[m, n/2 + j] =
+//                bf16(silu(gate_j) * up_j) for the 64-blocks of each 128 columns
+//   EPI_PARTIAL  swap-AB split-K partials, transposed: partial[split][n][m] = acc (M indexes weight rows and N
+//                tokens, so this writes Y[token][feature] partial sums for a consumer to reduce in a fixed order)
+//   EPI_BF16     out_bf16[m, n] = bf16(acc)
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "gemm.h"
+#include "ptx.cuh"
+
+namespace lrm {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int UMMA_K = 16;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                GemmArgs args) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t *empty = full + C::STAGES;
+    uint64_t *acc_full = empty + C::STAGES;
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int m_tiles = (args.M + BM - 1) / BM, n_tiles = (args.N + BN - 1) / BN;
+    const int nkb = (args.K + BK - 1) / BK;
+    const int kbps = args.kb_per_split;
+    const int total = m_tiles * n_tiles * args.splits;
+    uint32_t *err = args.err;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            ptx::mbar_init(&acc_full[a], 1);
+            ptx::mbar_init(&acc_empty[a], 4);
+        }
+        ptx::mbar_init(mma_done, 1);
+        ptx::fence_barrier_init();
+        ptx::prefetch_tmap(&tmap_a);
+        ptx::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // Tile t -> (split, m block, n block); n is fastest so consecutive CTAs share the A rows.
+    auto decode_tile = [&](int t, int &split, int &mb, int &nb) {
+        split = t / (m_tiles * n_tiles);
+        int r = t % (m_tiles * n_tiles);
+        mb = r / n_tiles;
+        nb = r % n_tiles;
+    };
+    auto kb_range = [&](int split, int &k0, int &k1) {
+        k0 = split * kbps;
+        k1 = min(nkb, k0 + kbps);
+    };
+
+    if (warp == 0) {
+        if (ptx::elect_one()) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int split, mb, nb, k0, k1;
+                decode_tile(t, split, mb, nb);
+                kb_range(split, k0, k1);
+                for (int kb = k0; kb < k1; ++kb, ++it) {
+                    int s = it % C::STAGES;
+                    uint32_t ph = (it / C::STAGES) & 1;
+                    if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, 0x1001)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + s * C::STAGE_BYTES;
+                    uint8_t *sb = sa + C::A_BYTES;
+                    ptx::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+                    ptx::tma_load_2d(sa, &tmap_a, &full[s], kb * BK, mb * BM);
+                    ptx::tma_load_2d(sb, &tmap_b, &full[s], kb * BK, nb * BN);
+                }
+            }
+            // Let every load this thread issued land before the CTA can exit (normally they all have).
+            uint32_t first = it > (uint32_t)C::STAGES ? it - C::STAGES : 0;
+            for (uint32_t j = first; j < it; ++j)
+                ptx::mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, err, 0x1002);
+        }
+    } else if (warp == 1) {
+        if (ptx::elect_one()) {
+            constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
+            uint32_t it = 0, local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+                int split, mb, nb, k0, k1;
+                decode_tile(t, split, mb, nb);
+                kb_range(split, k0, k1);
+                const int a = local & 1;
+                if (!ptx::mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, err, 0x1003)) break;
+                ptx::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + a * BN;
+                for (int kb = k0; kb < k1; ++kb, ++it) {
+                    int s = it % C::STAGES;
+                    if (!ptx::mbar_wait(&full[s], (it / C::STAGES) & 1, err, 0x1004)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    uint32_t sa = ptx::smem_u32(smem + s * C::STAGE_BYTES);
+                    uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        uint64_t da = ptx::sw128_kmajor_desc(sa + k * UMMA_K * 2);
+                        uint64_t db = ptx::sw128_kmajor_desc(sb + k * UMMA_K * 2);
+                        ptx::mma_bf16(d_tmem, da, db, idesc, (kb > k0 || k > 0) ? 1u : 0u);
+                    }
+                    ptx::mma_commit(&empty[s]);
+                }
+                ptx::mma_commit(&acc_full[a]);
+            }
+            ptx::mma_commit(mma_done);
+            ptx::mbar_wait(mma_done, 0, err, 0x1005);
+        }
+    } else {
+        // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds rows 32q..32q+31 of the tile.
+        const int q = warp & 3;
+        uint32_t local = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+            int split, mb, nb, k0, k1;
+            decode_tile(t, split, mb, nb);
+            kb_range(split, k0, k1);
+            const int a = local & 1;
+            if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1006)) break;
+            ptx::tc_fence_after();
+            const int row = mb * BM + q * 32 + lane;  // M index
+            const uint32_t t_row = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
+            const int n0 = nb * BN;
+            const bool has_k = k1 > k0;
+            if (EPI == EPI_SWIGLU) {
+                for (int b = 0; b < BN / 128; ++b) {
+#pragma unroll 1
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t g[16], u[16];
+                        ptx::tmem_ld16(t_row + b * 128 + j * 16, g);
+                        ptx::tmem_ld16(t_row + b * 128 + 64 + j * 16, u);
+                        ptx::tmem_ld_wait();
+                        if (row < args.M && n0 + b * 128 < args.N) {
+                            uint32_t packed[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                float g0 = has_k ? __uint_as_float(g[2 * e]) : 0.f;
+                                float g1 = has_k ? __uint_as_float(g[2 * e + 1]) : 0.f;
+                                float u0 = has_k ? __uint_as_float(u[2 * e]) : 0.f;
+                                float u1 = has_k ? __uint_as_float(u[2 * e + 1]) : 0.f;
+                                packed[e] = pack_bf16(silu_f(g0) * u0, silu_f(g1) * u1);
+                            }
+                            __nv_bfloat16 *dst = args.out_bf16 + (size_t)row * args.ldo + (n0 + b * 128) / 2 + j * 16;
+                            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+                            d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                            d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 16; ++c) {
+                    uint32_t v[16];
+                    ptx::tmem_ld16(t_row + c * 16, v);
+                    ptx::tmem_ld_wait();
+                    if (!has_k)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] = 0;
+                    const int col = n0 + c * 16;
+                    if (col >= args.N) continue;
+                    const int ncols = min(16, args.N - col);
+                    if (EPI == EPI_PARTIAL) {
+                        if (row < args.M) {
+                            float *p = args.partial + (size_t)split * args.split_stride + (size_t)col * args.ldo + row;
+#pragma unroll
+                            for (int e = 0; e < 16; ++e)
+                                if (e < ncols) p[(size_t)e * args.ldo] = __uint_as_float(v[e]);
+                        }
+                    } else if (row < args.M) {
+                        if (EPI == EPI_BF16) {
+                            __nv_bfloat16 *dst = args.out_bf16 + (size_t)row * args.ldo + col;
+                            if (ncols == 16) {
+                                uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+                                d4[0] = make_uint4(pack_bf16(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                                                   pack_bf16(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                                                   pack_bf16(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                                                   pack_bf16(__uint_as_float(v[6]), __uint_as_float(v[7])));
+                                d4[1] = make_uint4(pack_bf16(__uint_as_float(v[8]), __uint_as_float(v[9])),
+                                                   pack_bf16(__uint_as_float(v[10]), __uint_as_float(v[11])),
+                                                   pack_bf16(__uint_as_float(v[12]), __uint_as_float(v[13])),
+                                                   pack_bf16(__uint_as_float(v[14]), __uint_as_float(v[15])));
+                            } else {
+                                for (int e = 0; e < ncols; ++e) dst[e] = __float2bfloat16_rn(__uint_as_float(v[e]));
+                            }
+                        } else {
+                            float *dst = args.out_f32 + (size_t)row * args.ldo + col;
+                            float f[16];
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+                            if (EPI == EPI_RESID) {
+                                const float *r = args.resid + (size_t)row * args.ldr + col;
+                                if (ncols == 16) {
+#pragma unroll
+                                    for (int e4 = 0; e4 < 4; ++e4) {
+                                        float4 rv = reinterpret_cast<const float4 *>(r)[e4];
+                                        f[4 * e4 + 0] += rv.x;
+                                        f[4 * e4 + 1] += rv.y;
+                                        f[4 * e4 + 2] += rv.z;
+                                        f[4 * e4 + 3] += rv.w;
+                                    }
+                                } else {
+                                    for (int e = 0; e < ncols; ++e) f[e] += r[e];
+                                }
+                            }
+                            if (ncols == 16) {
+                                float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+                                for (int e4 = 0; e4 < 4; ++e4)
+                                    d4[e4] = make_float4(f[4 * e4], f[4 * e4 + 1], f[4 * e4 + 2], f[4 * e4 + 3]);
+                            } else {
+                                for (int e = 0; e < ncols; ++e) dst[e] = f[e];
+                            }
+                        }
+                    }
+                }
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&acc_empty[a]);
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    if (warp == 1) ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ---- host side --------------------------------------------------------------------------------------------------
+
+bool make_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    // bf16 [rows, cols] row-major: dim 0 = cols (inner), dim 1 = rows. Box {64, box_rows}, 128-byte swizzle.
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims,
+                                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int sms,
+                      cudaStream_t stream) {
+    using C = Cfg<BN>;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        configured[dev & 63] = true;
+    }
+    int m_tiles = (args.M + BM - 1) / BM, n_tiles = (args.N + BN - 1) / BN;
+    int total = m_tiles * n_tiles * args.splits;
+    int grid = total < sms ? total : sms;
+    gemm_kernel<BN, EPI><<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, args);
+    return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_epi(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int sms,
+                       cudaStream_t stream) {
+    switch (args.epi) {
+        case EPI_F32: return launch_bn<BN, EPI_F32>(ta, tb, args, sms, stream);
+        case EPI_RESID: return launch_bn<BN, EPI_RESID>(ta, tb, args, sms, stream);
+        case EPI_SWIGLU: return launch_bn<BN, EPI_SWIGLU>(ta, tb, args, sms, stream);
+        case EPI_PARTIAL: return launch_bn<BN, EPI_PARTIAL>(ta, tb, args, sms, stream);
+        case EPI_BF16: return launch_bn<BN, EPI_BF16>(ta, tb, args, sms, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+const char *gemm_check(const GemmArgs &a) {
+    if (a.M < 1 || a.N < 1 || a.K < 1) return "M, N and K must be positive";
+    if (a.K % 8) return "K must be a multiple of 8 (16-byte rows for TMA)";
+    if (((uintptr_t)a.A & 15) || ((uintptr_t)a.B & 15)) return "A and B must be 16-byte aligned";
+    if (a.bn != 64 && a.bn != 128 && a.bn != 256) return "bn must be 64, 128 or 256";
+    if (a.splits < 1 || a.kb_per_split < 1) return "splits and kb_per_split must be positive";
+    int nkb = (a.K + BK - 1) / BK;
+    if ((long)a.splits * a.kb_per_split < nkb) return "splits * kb_per_split must cover K";
+    if (a.epi == EPI_SWIGLU && (a.N % 128 || a.bn < 128)) return "SwiGLU needs N % 128 == 0 and bn >= 128";
+    if (a.epi == EPI_SWIGLU && (a.ldo % 8 || ((uintptr_t)a.out_bf16 & 15))) return "SwiGLU output needs 16-byte rows";
+    if (a.epi != EPI_PARTIAL && a.splits != 1) return "split-K writes partials only (EPI_PARTIAL)";
+    if ((a.epi == EPI_F32 || a.epi == EPI_RESID) && (a.ldo % 4 || ((uintptr_t)a.out_f32 & 15)))
+        return "fp32 output needs 16-byte aligned rows";
+    if (a.epi == EPI_RESID && (a.ldr % 4 || ((uintptr_t)a.resid & 15))) return "resid needs 16-byte aligned rows";
+    if (a.epi == EPI_BF16 && (a.ldo % 8 || ((uintptr_t)a.out_bf16 & 15))) return "bf16 output needs 16-byte rows";
+    if (a.epi == EPI_PARTIAL && !a.partial) return "partial output missing";
+    if (!a.err) return "error word missing";
+    return nullptr;
+}
+
+cudaError_t gemm_launch(const GemmArgs &args, int sms, cudaStream_t stream) {
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, args.A, args.M, args.K, BM)) return cudaErrorInvalidValue;
+    if (!make_tmap_2d(&tb, args.B, args.N, args.K, args.bn)) return cudaErrorInvalidValue;
+    switch (args.bn) {
+        case 64: return launch_epi<64>(ta, tb, args, sms, stream);
+        case 128: return launch_epi<128>(ta, tb, args, sms, stream);
+        case 256: return launch_epi<256>(ta, tb, args, sms, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace lrm

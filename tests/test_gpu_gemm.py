@@ -1,0 +1,96 @@
+"""The tcgen05 GEMM (lrm_op_gemm_bf16) against an fp64 reference on the same bf16 inputs (GPU tier).
+
+fp32 accumulation in TMEM over k <= 3072 keeps the relative L2 error near 1e-6; the bound used is 2e-5 for fp32
+outputs and 1e-2 for bf16-rounded outputs (one bf16 rounding is 2^-9 relative)."""
+
+import pytest
+
+from tests.conftest import cuda_available
+
+pytestmark = pytest.mark.gpu
+
+if cuda_available():
+    import torch
+
+    from rosylnalive_b200 import ops
+
+
+def rel(a, b):
+    a = a.double()
+    b = b.double()
+    return ((a - b).norm() / b.norm().clamp_min(1e-300)).item()
+
+
+def bf16(shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device="cuda") * scale).to(torch.bfloat16)
+
+
+@pytest.fixture(autouse=True)
+def _device():
+    ops.set_device(0)
+    assert ops.error_word() == 0
+    yield
+    torch.cuda.synchronize()
+    assert ops.error_word() == 0
+
+
+@pytest.mark.parametrize("m,n,k,bn", [(256, 256, 1024, 256), (200, 192, 512, 64), (1, 4096, 1024, 128),
+                                      (384, 1024, 3072, 256), (130, 152, 64, 128), (4096, 2048, 1024, 256),
+                                      (17, 64, 136, 64)])
+def test_gemm_f32(m, n, k, bn):
+    a, b = bf16((m, k), seed=1), bf16((n, k), 0.05, seed=2)
+    out = torch.full((m, n), float("nan"), device="cuda")
+    ops.gemm(a, b, out, ops.GEMM_F32, bn=bn)
+    torch.cuda.synchronize()
+    ref = a.double() @ b.double().T
+    assert rel(out, ref) < 2e-5
+
+
+def test_gemm_resid_in_place():
+    m, n, k = 300, 1024, 2048
+    a, b = bf16((m, k), seed=3), bf16((n, k), 0.02, seed=4)
+    x = torch.randn(m, n, device="cuda")
+    ref = x.double() + a.double() @ b.double().T
+    ops.gemm(a, b, x, ops.GEMM_RESID, resid=x)
+    torch.cuda.synchronize()
+    assert rel(x, ref) < 2e-5
+
+
+def test_gemm_swiglu_interleaved():
+    m, n, k = 256, 768, 1024
+    a, b = bf16((m, k), seed=5), bf16((n, k), 0.05, seed=6)
+    out = torch.zeros(m, n // 2, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(a, b, out, ops.GEMM_SWIGLU, bn=256)
+    torch.cuda.synchronize()
+    y = a.double() @ b.double().T
+    y = y.view(m, n // 128, 2, 64)
+    g, u = y[:, :, 0, :], y[:, :, 1, :]
+    ref = (g * torch.sigmoid(g) * u).reshape(m, n // 2)
+    assert rel(out, ref) < 1e-2
+
+
+def test_gemm_split_k_partials_transposed():
+    feats, toks, k, splits = 4096, 64, 1024, 4
+    w, x = bf16((feats, k), 0.05, seed=7), bf16((toks, k), seed=8)
+    part = torch.full((splits, toks, feats), float("nan"), device="cuda")
+    ops.gemm(w, x, part, ops.GEMM_PARTIAL, splits=splits, bn=64, split_stride=toks * feats)
+    torch.cuda.synchronize()
+    ref = x.double() @ w.double().T
+    assert rel(part.sum(0), ref) < 2e-5
+
+
+def test_gemm_bf16_out():
+    m, n, k = 512, 1536, 1024
+    a, b = bf16((m, k), seed=9), bf16((n, k), 0.05, seed=10)
+    out = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(a, b, out, ops.GEMM_BF16)
+    torch.cuda.synchronize()
+    assert rel(out, a.double() @ b.double().T) < 1e-2
+
+
+def test_gemm_rejects_bad_arguments():
+    a, b = bf16((64, 100)), bf16((64, 100))
+    out = torch.zeros(64, 64, device="cuda")
+    with pytest.raises(ValueError):
+        ops.gemm(a, b, out)  # k = 100 is not a multiple of 8
