@@ -191,6 +191,72 @@ typedef struct lrm_gemm_desc {
 } lrm_gemm_desc;
 lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *desc);
 
+/* ---- the Qwen3 forward engine (bf16 fast path) ---------------------------------------------------------------- */
+/*
+ * The executor the reference plans but does not have (src/Lrm.Gpu.Exec/Placeholder.fs:1,
+ * src/Lrm.Models.Qwen/Placeholder.fs:1; schedule of tests/Lrm.Tensor.Tests/TinyModel.fs:144-236): a whole-model
+ * Qwen3 decoder forward on one device, bf16 weights and activations, fp32 residual stream and accumulation, bf16
+ * paged KV cache (16-token pages) shared by `max_seqs` sequence slots. Prefill runs sequences packed together; a
+ * decode step runs one token for each of `batch` slots. Host entry points copy their inputs in and results out;
+ * the *_graph / *_replay pair runs decode steps with every input resident on the device (ids fed back on device).
+ * Requirements: head_dim 128, q_heads = 2 kv_heads, hidden and intermediate multiples of 128.
+ */
+typedef struct lrm_qwen_s *lrm_qwen;
+
+typedef struct lrm_qwen_config {
+    int32_t layers, hidden, q_heads, kv_heads, head_dim, intermediate, vocab;
+    float eps;
+    int32_t max_pos;    /* longest sequence (RoPE table rows) */
+    int32_t max_seqs;   /* sequence slots */
+    int32_t kv_pages;   /* 16-token pages in the KV pool */
+    int32_t max_tokens; /* tokens of one prefill call */
+    int32_t max_batch;  /* rows of one decode step */
+} lrm_qwen_config;
+
+lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *config, lrm_qwen *out);
+lrm_status lrm_qwen_destroy(lrm_qwen q);
+
+/* Copies one HF-named bf16 weight (e.g. "model.layers.3.self_attn.q_proj.weight") from host memory into the engine's
+ * layout: q/k/v fused into one [q+2kv heads, hidden] matrix, gate/up interleaved in blocks of 64 rows. */
+lrm_status lrm_qwen_set_weight(lrm_qwen q, const char *name, const uint16_t *bf16, uint64_t count);
+
+/* The RoPE table (T_spec, lrm_rope_table), float32 [rows, half]. rows >= max_pos, half = head_dim / 2. */
+lrm_status lrm_qwen_set_rope(lrm_qwen q, const float *cos_t, const float *sin_t, int32_t rows, int32_t half);
+
+/* Frees a slot's pages and sets its length to 0. */
+lrm_status lrm_qwen_reset_seq(lrm_qwen q, int32_t slot);
+
+/* Makes sure slot holds pages for `tokens` positions (so later decode steps need no host work). */
+lrm_status lrm_qwen_reserve(lrm_qwen q, int32_t slot, int32_t tokens);
+
+/* Prefill of `nseq` fresh sequences into slots[i] with lens[i] tokens each, ids concatenated (host). Writes each
+ * sequence's next greedy id (host, [nseq]) and, when logits is not NULL, its last-row logits (host, [nseq, vocab]). */
+lrm_status lrm_qwen_prefill(lrm_qwen q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
+                            uint32_t *next_ids, float *logits);
+
+/* One decode step: token ids[b] (host) appended to slots[b]; next greedy ids (host, [batch]) and optional logits
+ * (host, [batch, vocab]). Uses the captured graph when one exists for the same slots. */
+lrm_status lrm_qwen_decode(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *ids, uint32_t *next_ids,
+                           float *logits);
+
+/* Captures the decode step for `slots` as a CUDA graph whose input ids are the previous step's outputs. */
+lrm_status lrm_qwen_decode_graph(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *first_ids);
+
+/* Replays the captured step `steps` times on the engine's stream (asynchronous; lrm_qwen_sync waits). */
+lrm_status lrm_qwen_decode_replay(lrm_qwen q, int32_t steps);
+
+/* Device ids of the last replayed step (host copy, [batch]). */
+lrm_status lrm_qwen_last_ids(lrm_qwen q, uint32_t *ids);
+
+/* Waits for the engine's stream; returns LRM_ERR_TIMEOUT when a kernel reported a bounded-wait timeout. */
+lrm_status lrm_qwen_sync(lrm_qwen q);
+
+/* The engine's CUDA stream (cudaStream_t), for event timing. */
+lrm_status lrm_qwen_stream(lrm_qwen q, void **stream);
+
+/* Current length of a slot. */
+lrm_status lrm_qwen_seq_len(lrm_qwen q, int32_t slot, int32_t *len);
+
 /* ---- host helpers ------------------------------------------------------------------------------------------- */
 
 /* T_spec (src/Lrm.Tensor.CpuReference/Rope.fs:163-251): cos/sin [max_pos, half] float32 with

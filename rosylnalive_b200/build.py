@@ -27,6 +27,9 @@ SOURCES = [
     "rope_host.cpp",
     "ops.cu",
     "gemm_tcgen05.cu",
+    "qwen_kernels.cu",
+    "flash_prefill.cu",
+    "qwen_engine.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -1,0 +1,91 @@
+// qwen.h -- the bf16 forward path's fused kernels (internal launch interface).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lrm {
+
+// Paged KV cache (bf16): per layer [pages][kv_heads][2 (K, V)][kPageTokens][head_dim]; one page of one head is a
+// contiguous 8 KiB block (K 4 KiB then V 4 KiB at head_dim 128), the unit the decode kernel streams.
+constexpr int kPageTokens = 16;
+constexpr int kHeadDim = 128;
+
+struct KvLayout {
+    __nv_bfloat16 *pool;      // this layer's pool
+    const int32_t *pages;     // page table [max_seqs][max_pages_per_seq]
+    int32_t max_pages_per_seq;
+    int32_t kv_heads;
+};
+
+__host__ __device__ inline size_t kv_page_elems(int kv_heads) { return (size_t)kv_heads * 2 * kPageTokens * kHeadDim; }
+
+// x[t] = widen(embed[ids[t]]) (fp32 residual); xn[t] = bf16(rmsnorm(x[t]) * w).
+cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
+                              const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st);
+
+// x[t] += sum_s partial[s][t] (splits >= 0; 0 = no add); xn[t] = bf16(rmsnorm(x[t]) * w).
+cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
+                              const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st);
+
+// From qkv = sum_s partial[s] ([T][q+2kv heads][128] fp32): q = rope(rmsnorm(q_head) * q_norm) -> q_out bf16,
+// k = rope(rmsnorm(k_head) * k_norm) and raw v -> bf16 into the paged cache at (tok_slot[t], tok_pos[t]) and, when
+// k_out/v_out are given, into contiguous [T][kv][128] copies.
+struct QkvArgs {
+    const float *qkv;
+    int splits;
+    size_t split_stride;
+    int T, q_heads, kv_heads;
+    const __nv_bfloat16 *q_norm, *k_norm;
+    float eps;
+    const float *cos_t, *sin_t;  // [max_pos][64]
+    const int32_t *tok_slot, *tok_pos;
+    KvLayout kv;
+    __nv_bfloat16 *q_out, *k_out, *v_out;
+};
+cudaError_t launch_qk_norm_rope_kv(const QkvArgs &a, cudaStream_t st);
+
+// act[t][j] = bf16(silu(g) * u) with g, u = sum_s partial[s][t] over the 64-interleaved gate/up columns.
+cudaError_t launch_swiglu_reduce(const float *partial, int splits, size_t split_stride, int T, int inter,
+                                 __nv_bfloat16 *act, cudaStream_t st);
+
+// Paged split-K decode attention: one query per sequence (row b, slot slots[b], seq_len[slot] keys including the new
+// one), GQA group 2, pages_per_split pages per CTA; then the combine writes out bf16 [B][q_heads][128].
+struct DecodeAttnArgs {
+    const __nv_bfloat16 *q;  // [B][q_heads][128]
+    KvLayout kv;
+    const int32_t *slots;    // [B]
+    const int32_t *seq_len;  // [max_seqs]
+    int B, q_heads;
+    int pages_per_split, max_splits;
+    float scale_log2;        // head_dim^-0.5 * log2(e)
+    float *part_o;           // [B][kv_heads][max_splits][2][128]
+    float *part_ml;          // [B][kv_heads][max_splits][2][2]
+    __nv_bfloat16 *out;      // [B][q_heads][128]
+    uint32_t *err;
+};
+cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st);
+
+// Causal prefill attention over contiguous q [T][q_heads][128], k/v [T][kv_heads][128] for sequences packed by
+// cu_seqlens (positions start at 0 in each); out bf16 [T][q_heads][128].
+struct PrefillAttnArgs {
+    const __nv_bfloat16 *q, *k, *v;
+    __nv_bfloat16 *out;
+    const int32_t *cu_seqlens;  // [nseq + 1]
+    int nseq, max_len, q_heads, kv_heads;
+    float scale_log2;
+};
+cudaError_t launch_prefill_attention(const PrefillAttnArgs &a, cudaStream_t st);
+
+// rows[r] = argmax of logits[r] ([R][V] fp32): lowest index of the maximum, 0xFFFFFFFF for a row holding a NaN.
+cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st);
+
+// dst[r] = src[idx[r]] for rows of `cols` bf16 (gathers the last row of each sequence for lm_head).
+cudaError_t launch_gather_rows(const __nv_bfloat16 *src, const int32_t *idx, int R, int cols, __nv_bfloat16 *dst,
+                               cudaStream_t st);
+
+// seq_len[slots[b]] += 1 for b < B (after a decode step's append).
+cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos, cudaStream_t st);
+
+}  // namespace lrm

@@ -1,0 +1,669 @@
+// qwen_engine.cu -- the Qwen3 decoder forward on one B200 (bf16 fast path), exported as lrm_qwen_* in lrm_cuda.h.
+//
+// It composes the forward of tests/Lrm.Tensor.Tests/TinyModel.fs:144-204 (embed; per layer input norm, q/k/v,
+// QK-norm, RoPE, KV append, causal GQA attention, o_proj + residual, post norm, gate/up, SwiGLU, down + residual;
+// final norm; tied lm_head; argmax) from the fused kernels:
+//
+//   prefill (T tokens of packed sequences)            decode step (B rows, one token each)
+//   embed_norm                                        advance (positions, lengths) ; embed_norm
+//   per layer:                                        per layer:
+//     GEMM xn.Wqkv^T -> qkv fp32                        GEMM Wqkv.xn^T split-K -> partials
+//     qk_norm_rope_kv -> q, k, v (+ paged cache)        qk_norm_rope_kv (reduces the splits)
+//     flash prefill attention -> attn                   paged split-K decode attention + combine
+//     GEMM attn.Wo^T, epilogue x += .                   GEMM Wo.attn^T split-K ; resid_norm (x += sum; norm)
+//     resid_norm (post norm) -> xn                      GEMM Wgu.xn^T split-K ; swiglu_reduce
+//     GEMM xn.Wgu^T, SwiGLU epilogue -> act             GEMM Wdown.act^T split-K ; resid_norm (next norm)
+//     GEMM act.Wdown^T, epilogue x += . ; resid_norm
+//   gather last rows ; lm_head GEMM ; argmax          lm_head GEMM ; argmax
+//
+// Decode GEMMs swap A and B (weights fill the 128-row tensor-core tile, the B <= 64 tokens are N) and split K so
+// every weight matrix is streamed by ~128 CTAs; the consumers reduce the splits in a fixed order. The decode step is
+// a fixed sequence of launches over device-resident inputs, so it is captured once as a CUDA graph and replayed.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/lrm_cuda.h"
+#include "gemm.h"
+#include "internal.h"
+#include "qwen.h"
+
+namespace lrm {
+uint32_t *device_error_word();
+int device_sms();
+}  // namespace lrm
+
+using namespace lrm;
+
+namespace {
+
+struct Layer {
+    __nv_bfloat16 *w_qkv, *w_o, *w_gu, *w_down;
+    __nv_bfloat16 *in_norm, *post_norm, *q_norm, *k_norm;
+};
+
+template <class T>
+T *carve(uint8_t *&p, size_t n) {
+    T *r = (T *)p;
+    p += (n * sizeof(T) + 255) & ~(size_t)255;
+    return r;
+}
+
+}  // namespace
+
+struct lrm_qwen_s {
+    lrm_qwen_config c;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int sms = 148;
+    uint32_t *err = nullptr;
+    std::string error;
+    // weights
+    uint8_t *wmem = nullptr;
+    __nv_bfloat16 *embed = nullptr, *final_norm = nullptr;
+    std::vector<Layer> layers;
+    float *cos_t = nullptr, *sin_t = nullptr;
+    bool rope_set = false;
+    // KV
+    __nv_bfloat16 *pool = nullptr;
+    size_t layer_pool_elems = 0;
+    int32_t *d_pages = nullptr, *d_seq_len = nullptr;
+    std::vector<int32_t> h_pages, h_seq_len;
+    std::vector<std::vector<int32_t>> slot_pages;
+    std::vector<int32_t> free_pages;
+    int maxp = 0;
+    // activations
+    uint8_t *amem = nullptr;
+    uint32_t *ids = nullptr, *next = nullptr;
+    int32_t *tok_slot = nullptr, *tok_pos = nullptr, *cu = nullptr, *last_idx = nullptr, *d_slots = nullptr;
+    float *x = nullptr, *qkv = nullptr, *partial = nullptr, *part_o = nullptr, *part_ml = nullptr;
+    __nv_bfloat16 *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
+                  *xl = nullptr;
+    size_t partial_elems = 0;
+    int max_splits_attn = 0;
+    int pps = 32;
+    // decode graph
+    cudaGraphExec_t graph = nullptr;
+    int graph_batch = 0;
+    std::vector<int32_t> graph_slots;
+    // staging
+    uint32_t *h_pinned = nullptr;
+    int qkv_rows = 0;
+};
+
+static lrm_status qfail(lrm_qwen q, lrm_status s, const std::string &m) {
+    if (q) q->error = m;
+    set_thread_error(m);
+    return s;
+}
+static lrm_status qcuda(lrm_qwen q, cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return LRM_OK;
+    return qfail(q, LRM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+#define QTRY(q, call, what)                              \
+    do {                                                 \
+        cudaError_t e_ = (call);                         \
+        if (e_ != cudaSuccess) return qcuda(q, e_, what); \
+    } while (0)
+
+// Split counts for the decode GEMMs: enough CTAs to stream each weight matrix with ~all SMs.
+static int choose_splits(int m_tiles, int kb, int sms) {
+    int s = (sms + m_tiles - 1) / m_tiles;
+    if (s > kb) s = kb;
+    if (s < 1) s = 1;
+    while (s > 1 && (kb + s - 1) / s * (s - 1) >= kb) --s;  // no empty split
+    return s;
+}
+
+static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, int K, int epi, int bn, int splits,
+                       void *out, int ldo, const float *resid, int ldr, size_t split_stride) {
+    GemmArgs a;
+    memset(&a, 0, sizeof a);
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.A = A;
+    a.B = B;
+    a.epi = epi;
+    a.bn = bn;
+    a.splits = splits;
+    int nkb = (K + 63) / 64;
+    a.kb_per_split = (nkb + splits - 1) / splits;
+    if (epi == EPI_SWIGLU || epi == EPI_BF16)
+        a.out_bf16 = (__nv_bfloat16 *)out;
+    else if (epi == EPI_PARTIAL)
+        a.partial = (float *)out;
+    else
+        a.out_f32 = (float *)out;
+    a.ldo = ldo;
+    a.resid = resid;
+    a.ldr = ldr;
+    a.split_stride = split_stride;
+    a.err = Q->err;
+    if (const char *why = gemm_check(a)) return qfail(Q, LRM_ERR_ARGUMENT, std::string("gemm: ") + why);
+    return qcuda(Q, gemm_launch(a, Q->sms, Q->stream), "gemm");
+}
+
+#define LTRY(expr)                      \
+    do {                                \
+        lrm_status s_ = (expr);         \
+        if (s_ != LRM_OK) return s_;    \
+    } while (0)
+#define KTRY(Q, call, what) QTRY(Q, call, what)
+
+// One decode step over device-resident ids/slots (Q->ids[0..B), Q->d_slots) -> Q->next; logits in Q->partial.
+static lrm_status decode_step(lrm_qwen Q, int B) {
+    const lrm_qwen_config &c = Q->c;
+    cudaStream_t st = Q->stream;
+    const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
+    const int nqkv = Q->qkv_rows;
+    KTRY(Q, launch_advance(Q->d_slots, B, Q->d_seq_len, Q->tok_pos, st), "advance");
+    KTRY(Q, launch_embed_norm(Q->ids, B, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
+         "embed_norm");
+    const int s_qkv = choose_splits((nqkv + 127) / 128, (H + 63) / 64, Q->sms);
+    const int s_o = choose_splits((H + 127) / 128, (qh * kHeadDim + 63) / 64, Q->sms);
+    const int s_gu = choose_splits((2 * I + 127) / 128, (H + 63) / 64, Q->sms);
+    const int s_d = choose_splits((H + 127) / 128, (I + 63) / 64, Q->sms);
+    for (int l = 0; l < c.layers; ++l) {
+        const Layer &L = Q->layers[l];
+        LTRY(gemm(Q, L.w_qkv, Q->xn, nqkv, B, H, EPI_PARTIAL, 64, s_qkv, Q->partial, nqkv, nullptr, 0,
+                  (size_t)B * nqkv));
+        QkvArgs qa;
+        qa.qkv = Q->partial;
+        qa.splits = s_qkv;
+        qa.split_stride = (size_t)B * nqkv;
+        qa.T = B;
+        qa.q_heads = qh;
+        qa.kv_heads = kvh;
+        qa.q_norm = L.q_norm;
+        qa.k_norm = L.k_norm;
+        qa.eps = c.eps;
+        qa.cos_t = Q->cos_t;
+        qa.sin_t = Q->sin_t;
+        qa.tok_slot = Q->d_slots;
+        qa.tok_pos = Q->tok_pos;
+        qa.kv = KvLayout{Q->pool + (size_t)l * Q->layer_pool_elems, Q->d_pages, Q->maxp, kvh};
+        qa.q_out = Q->q;
+        qa.k_out = nullptr;
+        qa.v_out = nullptr;
+        KTRY(Q, launch_qk_norm_rope_kv(qa, st), "qk_norm_rope_kv");
+        DecodeAttnArgs da;
+        da.q = Q->q;
+        da.kv = qa.kv;
+        da.slots = Q->d_slots;
+        da.seq_len = Q->d_seq_len;
+        da.B = B;
+        da.q_heads = qh;
+        da.pages_per_split = Q->pps;
+        da.max_splits = Q->max_splits_attn;
+        da.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+        da.part_o = Q->part_o;
+        da.part_ml = Q->part_ml;
+        da.out = Q->attn;
+        da.err = Q->err;
+        KTRY(Q, launch_decode_attention(da, st), "decode_attention");
+        LTRY(gemm(Q, L.w_o, Q->attn, H, B, qh * kHeadDim, EPI_PARTIAL, 64, s_o, Q->partial, H, nullptr, 0,
+                  (size_t)B * H));
+        KTRY(Q, launch_resid_norm(Q->x, Q->partial, s_o, (size_t)B * H, B, H, L.post_norm, c.eps, Q->xn, st),
+             "resid_norm");
+        LTRY(gemm(Q, L.w_gu, Q->xn, 2 * I, B, H, EPI_PARTIAL, 64, s_gu, Q->partial, 2 * I, nullptr, 0,
+                  (size_t)B * 2 * I));
+        KTRY(Q, launch_swiglu_reduce(Q->partial, s_gu, (size_t)B * 2 * I, B, I, Q->act, st), "swiglu_reduce");
+        LTRY(gemm(Q, L.w_down, Q->act, H, B, I, EPI_PARTIAL, 64, s_d, Q->partial, H, nullptr, 0, (size_t)B * H));
+        const __nv_bfloat16 *next_norm = l + 1 < c.layers ? Q->layers[l + 1].in_norm : Q->final_norm;
+        KTRY(Q, launch_resid_norm(Q->x, Q->partial, s_d, (size_t)B * H, B, H, next_norm, c.eps, Q->xn, st),
+             "resid_norm");
+    }
+    LTRY(gemm(Q, Q->embed, Q->xn, c.vocab, B, H, EPI_PARTIAL, 64, 1, Q->partial, c.vocab, nullptr, 0,
+              (size_t)B * c.vocab));
+    KTRY(Q, launch_argmax(Q->partial, B, c.vocab, Q->next, st), "argmax");
+    return LRM_OK;
+}
+
+static lrm_status check_ready(lrm_qwen Q) {
+    if (!Q) return qfail(nullptr, LRM_ERR_ARGUMENT, "engine is null");
+    if (!Q->rope_set) return qfail(Q, LRM_ERR_STATE, "set the RoPE table first");
+    cudaSetDevice(Q->device);
+    return LRM_OK;
+}
+
+static lrm_status sync_check(lrm_qwen Q) {
+    QTRY(Q, cudaStreamSynchronize(Q->stream), "stream");
+    uint32_t code = 0;
+    QTRY(Q, cudaMemcpy(&code, Q->err, 4, cudaMemcpyDeviceToHost), "error word");
+    if (code) {
+        cudaMemset(Q->err, 0, 4);
+        char buf[96];
+        snprintf(buf, sizeof buf, "a kernel's bounded wait gave up (code 0x%x)", code);
+        return qfail(Q, LRM_ERR_TIMEOUT, buf);
+    }
+    return LRM_OK;
+}
+
+static lrm_status upload_page_row(lrm_qwen Q, int slot) {
+    int32_t *row = &Q->h_pages[(size_t)slot * Q->maxp];
+    QTRY(Q, cudaMemcpyAsync(Q->d_pages + (size_t)slot * Q->maxp, row, sizeof(int32_t) * Q->maxp,
+                            cudaMemcpyHostToDevice, Q->stream),
+         "page table");
+    return sync_check(Q);
+}
+
+extern "C" {
+
+lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *cfg, lrm_qwen *out) {
+    if (!cfg || !out) return qfail(nullptr, LRM_ERR_ARGUMENT, "null argument");
+    *out = nullptr;
+    const lrm_qwen_config c = *cfg;
+    if (c.head_dim != kHeadDim) return qfail(nullptr, LRM_ERR_ARGUMENT, "the bf16 engine needs head_dim 128");
+    if (c.kv_heads < 1 || c.q_heads != 2 * c.kv_heads)
+        return qfail(nullptr, LRM_ERR_ARGUMENT, "the bf16 engine needs q_heads = 2 * kv_heads");
+    if (c.hidden % 128 || c.intermediate % 128 || c.hidden < 128)
+        return qfail(nullptr, LRM_ERR_ARGUMENT, "hidden and intermediate must be multiples of 128");
+    if (c.layers < 1 || c.vocab < 1 || c.max_pos < 1 || c.max_seqs < 1 || c.kv_pages < 1 || c.max_tokens < 1 ||
+        c.max_batch < 1 || c.max_batch > 65535)
+        return qfail(nullptr, LRM_ERR_ARGUMENT, "sizes must be positive");
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return qcuda(nullptr, e, "cudaSetDevice");
+    std::unique_ptr<lrm_qwen_s> Q(new lrm_qwen_s());
+    Q->c = c;
+    Q->device = device;
+    Q->err = device_error_word();
+    Q->sms = device_sms();
+    if (!Q->err) return LRM_ERR_CUDA;
+    QTRY(Q.get(), cudaStreamCreateWithFlags(&Q->stream, cudaStreamNonBlocking), "stream");
+    const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate, V = c.vocab;
+    Q->qkv_rows = (qh + 2 * kvh) * kHeadDim;
+    // weights
+    size_t per_layer = (size_t)Q->qkv_rows * H + (size_t)H * qh * kHeadDim + (size_t)2 * I * H + (size_t)H * I +
+                       2 * H + 2 * kHeadDim;
+    size_t wbytes = ((size_t)V * H + H) * 2 + (size_t)c.layers * (per_layer * 2 + 8 * 256) + 4096;
+    QTRY(Q.get(), cudaMalloc(&Q->wmem, wbytes), "weights");
+    QTRY(Q.get(), cudaMemset(Q->wmem, 0, wbytes), "weights");
+    uint8_t *p = Q->wmem;
+    Q->embed = carve<__nv_bfloat16>(p, (size_t)V * H);
+    Q->final_norm = carve<__nv_bfloat16>(p, H);
+    Q->layers.resize(c.layers);
+    for (auto &L : Q->layers) {
+        L.w_qkv = carve<__nv_bfloat16>(p, (size_t)Q->qkv_rows * H);
+        L.w_o = carve<__nv_bfloat16>(p, (size_t)H * qh * kHeadDim);
+        L.w_gu = carve<__nv_bfloat16>(p, (size_t)2 * I * H);
+        L.w_down = carve<__nv_bfloat16>(p, (size_t)H * I);
+        L.in_norm = carve<__nv_bfloat16>(p, H);
+        L.post_norm = carve<__nv_bfloat16>(p, H);
+        L.q_norm = carve<__nv_bfloat16>(p, kHeadDim);
+        L.k_norm = carve<__nv_bfloat16>(p, kHeadDim);
+    }
+    QTRY(Q.get(), cudaMalloc(&Q->cos_t, sizeof(float) * (size_t)c.max_pos * 64), "rope");
+    QTRY(Q.get(), cudaMalloc(&Q->sin_t, sizeof(float) * (size_t)c.max_pos * 64), "rope");
+    // KV pool and page tables
+    Q->maxp = (c.max_pos + kPageTokens - 1) / kPageTokens;
+    Q->layer_pool_elems = (size_t)c.kv_pages * kv_page_elems(kvh);
+    e = cudaMalloc(&Q->pool, Q->layer_pool_elems * c.layers * sizeof(__nv_bfloat16));
+    if (e != cudaSuccess) return qfail(Q.get(), LRM_ERR_OUT_OF_MEMORY, "KV pool allocation failed");
+    QTRY(Q.get(), cudaMemset(Q->pool, 0, Q->layer_pool_elems * c.layers * sizeof(__nv_bfloat16)), "KV pool");
+    QTRY(Q.get(), cudaMalloc(&Q->d_pages, sizeof(int32_t) * (size_t)c.max_seqs * Q->maxp), "pages");
+    QTRY(Q.get(), cudaMemset(Q->d_pages, 0, sizeof(int32_t) * (size_t)c.max_seqs * Q->maxp), "pages");
+    QTRY(Q.get(), cudaMalloc(&Q->d_seq_len, sizeof(int32_t) * c.max_seqs), "seq_len");
+    QTRY(Q.get(), cudaMemset(Q->d_seq_len, 0, sizeof(int32_t) * c.max_seqs), "seq_len");
+    Q->h_pages.assign((size_t)c.max_seqs * Q->maxp, 0);
+    Q->h_seq_len.assign(c.max_seqs, 0);
+    Q->slot_pages.resize(c.max_seqs);
+    for (int i = c.kv_pages - 1; i >= 0; --i) Q->free_pages.push_back(i);
+    // activations
+    const int T = c.max_tokens > c.max_batch ? c.max_tokens : c.max_batch;
+    const int R = c.max_batch > c.max_seqs ? c.max_batch : c.max_seqs;
+    Q->max_splits_attn = (Q->maxp + Q->pps - 1) / Q->pps;
+    size_t part = (size_t)R * V;
+    size_t dec = (size_t)16 * c.max_batch * (Q->qkv_rows > 2 * I ? Q->qkv_rows : 2 * I) * 2;
+    if (dec > part) part = dec;
+    Q->partial_elems = part;
+    size_t abytes = 0;
+    abytes += (size_t)T * 4 * 3 + (size_t)R * 4 * 3 + (size_t)(c.max_seqs + 1) * 4 * 2;
+    abytes += (size_t)T * H * 4 + (size_t)T * Q->qkv_rows * 4 + part * 4;
+    abytes += (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * (128 + 2) * 4;
+    abytes += (size_t)T * (H + qh * kHeadDim * 2 + 2 * kvh * kHeadDim + I) * 2 + (size_t)R * H * 2;
+    abytes += 64 * 256;
+    QTRY(Q.get(), cudaMalloc(&Q->amem, abytes), "activations");
+    p = Q->amem;
+    Q->ids = carve<uint32_t>(p, T);
+    Q->tok_slot = carve<int32_t>(p, T);
+    Q->tok_pos = carve<int32_t>(p, T);
+    Q->next = carve<uint32_t>(p, R);
+    Q->last_idx = carve<int32_t>(p, R);
+    Q->d_slots = carve<int32_t>(p, R);
+    Q->cu = carve<int32_t>(p, c.max_seqs + 1);
+    Q->x = carve<float>(p, (size_t)T * H);
+    Q->qkv = carve<float>(p, (size_t)T * Q->qkv_rows);
+    Q->partial = carve<float>(p, part);
+    Q->part_o = carve<float>(p, (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * 128);
+    Q->part_ml = carve<float>(p, (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * 2);
+    Q->xn = carve<__nv_bfloat16>(p, (size_t)T * H);
+    Q->q = carve<__nv_bfloat16>(p, (size_t)T * qh * kHeadDim);
+    Q->k = carve<__nv_bfloat16>(p, (size_t)T * kvh * kHeadDim);
+    Q->v = carve<__nv_bfloat16>(p, (size_t)T * kvh * kHeadDim);
+    Q->attn = carve<__nv_bfloat16>(p, (size_t)T * qh * kHeadDim);
+    Q->act = carve<__nv_bfloat16>(p, (size_t)T * I);
+    Q->xl = carve<__nv_bfloat16>(p, (size_t)R * H);
+    if ((size_t)(p - Q->amem) > abytes) return qfail(Q.get(), LRM_ERR_STATE, "activation plan overflow");
+    QTRY(Q.get(), cudaMallocHost(&Q->h_pinned, sizeof(uint32_t) * (size_t)T * 4), "pinned staging");
+    *out = Q.release();
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_destroy(lrm_qwen Q) {
+    if (!Q) return LRM_ERR_ARGUMENT;
+    cudaSetDevice(Q->device);
+    cudaStreamSynchronize(Q->stream);
+    if (Q->graph) cudaGraphExecDestroy(Q->graph);
+    cudaFree(Q->wmem);
+    cudaFree(Q->cos_t);
+    cudaFree(Q->sin_t);
+    cudaFree(Q->pool);
+    cudaFree(Q->d_pages);
+    cudaFree(Q->d_seq_len);
+    cudaFree(Q->amem);
+    cudaFreeHost(Q->h_pinned);
+    cudaStreamDestroy(Q->stream);
+    delete Q;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_set_weight(lrm_qwen Q, const char *name, const uint16_t *w, uint64_t count) {
+    if (!Q || !name || !w) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
+    cudaSetDevice(Q->device);
+    const lrm_qwen_config &c = Q->c;
+    const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
+    std::string n(name);
+    auto put = [&](void *dst, uint64_t expect) -> lrm_status {
+        if (count != expect) return qfail(Q, LRM_ERR_ARGUMENT, n + ": wrong element count");
+        QTRY(Q, cudaMemcpy(dst, w, count * 2, cudaMemcpyHostToDevice), "set_weight");
+        return LRM_OK;
+    };
+    if (n == "model.embed_tokens.weight") return put(Q->embed, (uint64_t)c.vocab * H);
+    if (n == "model.norm.weight") return put(Q->final_norm, H);
+    int layer = -1, consumed = 0;
+    if (sscanf(name, "model.layers.%d.%n", &layer, &consumed) != 1 || consumed == 0 || layer < 0 || layer >= c.layers)
+        return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name of this model");
+    Layer &L = Q->layers[layer];
+    std::string rest = n.substr(consumed);
+    if (rest == "input_layernorm.weight") return put(L.in_norm, H);
+    if (rest == "post_attention_layernorm.weight") return put(L.post_norm, H);
+    if (rest == "self_attn.q_norm.weight") return put(L.q_norm, kHeadDim);
+    if (rest == "self_attn.k_norm.weight") return put(L.k_norm, kHeadDim);
+    if (rest == "self_attn.q_proj.weight") return put(L.w_qkv, (uint64_t)qh * kHeadDim * H);
+    if (rest == "self_attn.k_proj.weight") return put(L.w_qkv + (size_t)qh * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
+    if (rest == "self_attn.v_proj.weight")
+        return put(L.w_qkv + (size_t)(qh + kvh) * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
+    if (rest == "self_attn.o_proj.weight") return put(L.w_o, (uint64_t)H * qh * kHeadDim);
+    if (rest == "mlp.down_proj.weight") return put(L.w_down, (uint64_t)H * I);
+    if (rest == "mlp.gate_proj.weight" || rest == "mlp.up_proj.weight") {
+        if (count != (uint64_t)I * H) return qfail(Q, LRM_ERR_ARGUMENT, n + ": wrong element count");
+        const int off = rest == "mlp.gate_proj.weight" ? 0 : 64;
+        // rows j of gate/up go to row (j / 64) * 128 + off + j % 64: 64-row blocks, interleaved.
+        QTRY(Q, cudaMemcpy2D(L.w_gu + (size_t)off * H, (size_t)128 * H * 2, w, (size_t)64 * H * 2, (size_t)64 * H * 2,
+                             I / 64, cudaMemcpyHostToDevice),
+             "set_weight");
+        return LRM_OK;
+    }
+    return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name");
+}
+
+lrm_status lrm_qwen_set_rope(lrm_qwen Q, const float *cs, const float *sn, int32_t rows, int32_t half) {
+    if (!Q || !cs || !sn) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
+    if (half != 64 || rows < Q->c.max_pos) return qfail(Q, LRM_ERR_ARGUMENT, "the table must be [>= max_pos, 64]");
+    cudaSetDevice(Q->device);
+    QTRY(Q, cudaMemcpy(Q->cos_t, cs, sizeof(float) * (size_t)Q->c.max_pos * 64, cudaMemcpyHostToDevice), "rope");
+    QTRY(Q, cudaMemcpy(Q->sin_t, sn, sizeof(float) * (size_t)Q->c.max_pos * 64, cudaMemcpyHostToDevice), "rope");
+    Q->rope_set = true;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_reset_seq(lrm_qwen Q, int32_t slot) {
+    if (!Q || slot < 0 || slot >= Q->c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "slot out of range");
+    cudaSetDevice(Q->device);
+    for (int32_t pg : Q->slot_pages[slot]) Q->free_pages.push_back(pg);
+    Q->slot_pages[slot].clear();
+    std::fill(Q->h_pages.begin() + (size_t)slot * Q->maxp, Q->h_pages.begin() + (size_t)(slot + 1) * Q->maxp, 0);
+    Q->h_seq_len[slot] = 0;
+    int32_t zero = 0;
+    QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slot, &zero, 4, cudaMemcpyHostToDevice, Q->stream), "seq_len");
+    return upload_page_row(Q, slot);
+}
+
+lrm_status lrm_qwen_reserve(lrm_qwen Q, int32_t slot, int32_t tokens) {
+    if (!Q || slot < 0 || slot >= Q->c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "slot out of range");
+    if (tokens > Q->c.max_pos) return qfail(Q, LRM_ERR_ARGUMENT, "tokens beyond max_pos");
+    cudaSetDevice(Q->device);
+    int need = (tokens + kPageTokens - 1) / kPageTokens;
+    auto &pg = Q->slot_pages[slot];
+    bool changed = false;
+    while ((int)pg.size() < need) {
+        if (Q->free_pages.empty()) return qfail(Q, LRM_ERR_OUT_OF_MEMORY, "the KV pool has no free page");
+        int32_t id = Q->free_pages.back();
+        Q->free_pages.pop_back();
+        Q->h_pages[(size_t)slot * Q->maxp + pg.size()] = id;
+        pg.push_back(id);
+        changed = true;
+    }
+    return changed ? upload_page_row(Q, slot) : LRM_OK;
+}
+
+lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
+                            uint32_t *next_ids, float *logits) {
+    LTRY(check_ready(Q));
+    const lrm_qwen_config &c = Q->c;
+    if (nseq < 1 || nseq > c.max_seqs || !slots || !lens || !ids || !next_ids)
+        return qfail(Q, LRM_ERR_ARGUMENT, "bad prefill arguments");
+    std::vector<int32_t> cu(nseq + 1, 0), last(nseq), tslot, tpos;
+    int max_len = 0;
+    for (int i = 0; i < nseq; ++i) {
+        if (lens[i] < 1 || lens[i] > c.max_pos || slots[i] < 0 || slots[i] >= c.max_seqs)
+            return qfail(Q, LRM_ERR_ARGUMENT, "bad sequence length or slot");
+        cu[i + 1] = cu[i] + lens[i];
+        last[i] = cu[i + 1] - 1;
+        if (lens[i] > max_len) max_len = lens[i];
+    }
+    const int T = cu[nseq];
+    if (T > c.max_tokens) return qfail(Q, LRM_ERR_ARGUMENT, "more tokens than max_tokens");
+    for (int i = 0; i < nseq; ++i) {
+        if (uint32_t(slots[i]) >= (uint32_t)c.max_seqs) return LRM_ERR_ARGUMENT;
+        LTRY(lrm_qwen_reset_seq(Q, slots[i]));
+        LTRY(lrm_qwen_reserve(Q, slots[i], lens[i]));
+        for (int t = 0; t < lens[i]; ++t) {
+            tslot.push_back(slots[i]);
+            tpos.push_back(t);
+        }
+        Q->h_seq_len[slots[i]] = lens[i];
+    }
+    for (int i = 0; i < T; ++i)
+        if (ids[i] >= (uint32_t)c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
+    cudaStream_t st = Q->stream;
+    QTRY(Q, cudaMemcpyAsync(Q->ids, ids, 4 * (size_t)T, cudaMemcpyHostToDevice, st), "ids");
+    QTRY(Q, cudaMemcpyAsync(Q->tok_slot, tslot.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "slots");
+    QTRY(Q, cudaMemcpyAsync(Q->tok_pos, tpos.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "positions");
+    QTRY(Q, cudaMemcpyAsync(Q->cu, cu.data(), 4 * (size_t)(nseq + 1), cudaMemcpyHostToDevice, st), "cu_seqlens");
+    QTRY(Q, cudaMemcpyAsync(Q->last_idx, last.data(), 4 * (size_t)nseq, cudaMemcpyHostToDevice, st), "last rows");
+    for (int i = 0; i < nseq; ++i)
+        QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slots[i], &lens[i], 4, cudaMemcpyHostToDevice, st), "seq_len");
+    const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
+    KTRY(Q, launch_embed_norm(Q->ids, T, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
+         "embed_norm");
+    for (int l = 0; l < c.layers; ++l) {
+        const Layer &L = Q->layers[l];
+        LTRY(gemm(Q, Q->xn, L.w_qkv, T, Q->qkv_rows, H, EPI_F32, 256, 1, Q->qkv, Q->qkv_rows, nullptr, 0, 0));
+        QkvArgs qa;
+        qa.qkv = Q->qkv;
+        qa.splits = 1;
+        qa.split_stride = 0;
+        qa.T = T;
+        qa.q_heads = qh;
+        qa.kv_heads = kvh;
+        qa.q_norm = L.q_norm;
+        qa.k_norm = L.k_norm;
+        qa.eps = c.eps;
+        qa.cos_t = Q->cos_t;
+        qa.sin_t = Q->sin_t;
+        qa.tok_slot = Q->tok_slot;
+        qa.tok_pos = Q->tok_pos;
+        qa.kv = KvLayout{Q->pool + (size_t)l * Q->layer_pool_elems, Q->d_pages, Q->maxp, kvh};
+        qa.q_out = Q->q;
+        qa.k_out = Q->k;
+        qa.v_out = Q->v;
+        KTRY(Q, launch_qk_norm_rope_kv(qa, st), "qk_norm_rope_kv");
+        PrefillAttnArgs pa;
+        pa.q = Q->q;
+        pa.k = Q->k;
+        pa.v = Q->v;
+        pa.out = Q->attn;
+        pa.cu_seqlens = Q->cu;
+        pa.nseq = nseq;
+        pa.max_len = max_len;
+        pa.q_heads = qh;
+        pa.kv_heads = kvh;
+        pa.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+        KTRY(Q, launch_prefill_attention(pa, st), "prefill_attention");
+        LTRY(gemm(Q, Q->attn, L.w_o, T, H, qh * kHeadDim, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
+        KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, L.post_norm, c.eps, Q->xn, st), "resid_norm");
+        LTRY(gemm(Q, Q->xn, L.w_gu, T, 2 * I, H, EPI_SWIGLU, 256, 1, Q->act, I, nullptr, 0, 0));
+        LTRY(gemm(Q, Q->act, L.w_down, T, H, I, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
+        const __nv_bfloat16 *next_norm = l + 1 < c.layers ? Q->layers[l + 1].in_norm : Q->final_norm;
+        KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, next_norm, c.eps, Q->xn, st), "resid_norm");
+    }
+    KTRY(Q, launch_gather_rows(Q->xn, Q->last_idx, nseq, H, Q->xl, st), "gather");
+    LTRY(gemm(Q, Q->embed, Q->xl, c.vocab, nseq, H, EPI_PARTIAL, 64, 1, Q->partial, c.vocab, nullptr, 0,
+              (size_t)nseq * c.vocab));
+    KTRY(Q, launch_argmax(Q->partial, nseq, c.vocab, Q->next, st), "argmax");
+    QTRY(Q, cudaMemcpyAsync(next_ids, Q->next, 4 * (size_t)nseq, cudaMemcpyDeviceToHost, st), "next ids");
+    if (logits)
+        QTRY(Q, cudaMemcpyAsync(logits, Q->partial, 4 * (size_t)nseq * c.vocab, cudaMemcpyDeviceToHost, st), "logits");
+    return sync_check(Q);
+}
+
+static lrm_status set_slots(lrm_qwen Q, int32_t batch, const int32_t *slots) {
+    const lrm_qwen_config &c = Q->c;
+    if (batch < 1 || batch > c.max_batch || !slots) return qfail(Q, LRM_ERR_ARGUMENT, "bad batch");
+    for (int b = 0; b < batch; ++b) {
+        const int s = slots[b];
+        if (s < 0 || s >= c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "slot out of range");
+        for (int b2 = 0; b2 < b; ++b2)
+            if (slots[b2] == s) return qfail(Q, LRM_ERR_ARGUMENT, "a slot appears twice in one step");
+    }
+    QTRY(Q, cudaMemcpyAsync(Q->d_slots, slots, 4 * (size_t)batch, cudaMemcpyHostToDevice, Q->stream), "slots");
+    return LRM_OK;
+}
+
+// Host-side checks before a step: every slot must have a page for its next position.
+static lrm_status ensure_pages(lrm_qwen Q, int32_t batch, const int32_t *slots, int steps) {
+    for (int b = 0; b < batch; ++b) {
+        const int s = slots[b];
+        if (Q->h_seq_len[s] < 1) return qfail(Q, LRM_ERR_STATE, "decode needs a prefilled slot");
+        const int need = Q->h_seq_len[s] + steps;
+        if (need > Q->c.max_pos) return qfail(Q, LRM_ERR_ARGUMENT, "the sequence would pass max_pos");
+        LTRY(lrm_qwen_reserve(Q, s, need));
+    }
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_decode(lrm_qwen Q, int32_t batch, const int32_t *slots, const uint32_t *ids, uint32_t *next_ids,
+                           float *logits) {
+    LTRY(check_ready(Q));
+    if (!ids || !next_ids) return qfail(Q, LRM_ERR_ARGUMENT, "null ids");
+    for (int b = 0; b < batch; ++b)
+        if (ids[b] >= (uint32_t)Q->c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
+    LTRY(set_slots(Q, batch, slots));
+    LTRY(ensure_pages(Q, batch, slots, 1));
+    cudaStream_t st = Q->stream;
+    memcpy(Q->h_pinned, ids, 4 * (size_t)batch);
+    QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, st), "ids");
+    const bool use_graph = Q->graph && Q->graph_batch == batch &&
+                           std::equal(Q->graph_slots.begin(), Q->graph_slots.end(), slots);
+    if (use_graph) {
+        QTRY(Q, cudaGraphLaunch(Q->graph, st), "graph launch");
+    } else {
+        LTRY(decode_step(Q, batch));
+    }
+    QTRY(Q, cudaMemcpyAsync(Q->h_pinned + batch, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToHost, st), "next");
+    if (logits)
+        QTRY(Q, cudaMemcpyAsync(logits, Q->partial, 4 * (size_t)batch * Q->c.vocab, cudaMemcpyDeviceToHost, st),
+             "logits");
+    LTRY(sync_check(Q));
+    memcpy(next_ids, Q->h_pinned + batch, 4 * (size_t)batch);
+    for (int b = 0; b < batch; ++b) Q->h_seq_len[slots[b]] += 1;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots, const uint32_t *first_ids) {
+    LTRY(check_ready(Q));
+    LTRY(set_slots(Q, batch, slots));
+    if (first_ids) {
+        memcpy(Q->h_pinned, first_ids, 4 * (size_t)batch);
+        QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, Q->stream), "ids");
+    }
+    LTRY(sync_check(Q));
+    if (Q->graph) {
+        cudaGraphExecDestroy(Q->graph);
+        Q->graph = nullptr;
+    }
+    cudaGraph_t g;
+    QTRY(Q, cudaStreamBeginCapture(Q->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    lrm_status s = decode_step(Q, batch);
+    if (s == LRM_OK) {
+        cudaError_t e = cudaMemcpyAsync(Q->ids, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToDevice, Q->stream);
+        if (e != cudaSuccess) s = qcuda(Q, e, "feedback copy");
+    }
+    cudaError_t e = cudaStreamEndCapture(Q->stream, &g);
+    if (s != LRM_OK) return s;
+    QTRY(Q, e, "end capture");
+    e = cudaGraphInstantiate(&Q->graph, g, 0);
+    cudaGraphDestroy(g);
+    QTRY(Q, e, "graph instantiate");
+    Q->graph_batch = batch;
+    Q->graph_slots.assign(slots, slots + batch);
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_decode_replay(lrm_qwen Q, int32_t steps) {
+    LTRY(check_ready(Q));
+    if (!Q->graph) return qfail(Q, LRM_ERR_STATE, "no decode graph captured");
+    LTRY(ensure_pages(Q, Q->graph_batch, Q->graph_slots.data(), steps));
+    for (int i = 0; i < steps; ++i) QTRY(Q, cudaGraphLaunch(Q->graph, Q->stream), "graph launch");
+    for (int b = 0; b < Q->graph_batch; ++b) Q->h_seq_len[Q->graph_slots[b]] += steps;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_last_ids(lrm_qwen Q, uint32_t *ids) {
+    if (!Q || !ids) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
+    cudaSetDevice(Q->device);
+    LTRY(sync_check(Q));
+    QTRY(Q, cudaMemcpy(ids, Q->next, 4 * (size_t)(Q->graph_batch ? Q->graph_batch : 1), cudaMemcpyDeviceToHost),
+         "ids");
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_sync(lrm_qwen Q) {
+    if (!Q) return LRM_ERR_ARGUMENT;
+    cudaSetDevice(Q->device);
+    return sync_check(Q);
+}
+
+lrm_status lrm_qwen_stream(lrm_qwen Q, void **stream) {
+    if (!Q || !stream) return LRM_ERR_ARGUMENT;
+    *stream = (void *)Q->stream;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_seq_len(lrm_qwen Q, int32_t slot, int32_t *len) {
+    if (!Q || !len || slot < 0 || slot >= Q->c.max_seqs) return LRM_ERR_ARGUMENT;
+    cudaSetDevice(Q->device);
+    LTRY(sync_check(Q));
+    QTRY(Q, cudaMemcpy(len, Q->d_seq_len + slot, 4, cudaMemcpyDeviceToHost), "seq_len");
+    return LRM_OK;
+}
+
+}  // extern "C"

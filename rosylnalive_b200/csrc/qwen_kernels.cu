@@ -1,0 +1,500 @@
+// qwen_kernels.cu -- the bf16 forward path's fused element-wise/row kernels and the paged split-K decode attention.
+//
+// The reference computes these as separate catalog dispatches (embed_gather_bf16, rmsnorm_rows, rope_apply,
+// copy_rows, silu_mul, add, argmax_rows: src/Lrm.Shaders/hlsl/kernels/basic/*.hlsl). Here each neighbourhood is one
+// kernel so an activation makes one trip through HBM:
+//   embed_norm        embed gather + layer 0's input RMSNorm
+//   resid_norm        split-K reduce of o_proj/down + residual add + the next RMSNorm (decode)
+//   qk_norm_rope_kv   split-K reduce of q/k/v + per-head QK-RMSNorm + RoPE (T_spec table) + paged KV append
+//   swiglu_reduce     split-K reduce of gate/up + SwiGLU (decode)
+// and decode attention streams the paged bf16 KV cache with bulk async copies (see decode_attn_kernel).
+#include <cuda_bf16.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "ptx.cuh"
+#include "qwen.h"
+
+namespace lrm {
+namespace {
+
+constexpr unsigned FULL = 0xFFFFFFFFu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+// Sum over the 256 threads of a block; `red` holds 8 floats.
+__device__ __forceinline__ float block_sum256(float v, float *red) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i];
+    __syncthreads();
+    return t;
+}
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+
+// ---- embed + norm -------------------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t *ids, const __nv_bfloat16 *embed, int hidden,
+                                                         int vocab, const __nv_bfloat16 *w, float eps, float *x,
+                                                         __nv_bfloat16 *xn) {
+    __shared__ float red[8];
+    const int t = blockIdx.x;
+    uint32_t id = ids[t];
+    const bool ok = id < (uint32_t)vocab;
+    const __nv_bfloat16 *row = embed + (size_t)(ok ? id : 0) * hidden;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < hidden; c += 256) {
+        float v = ok ? bf(row[c]) : __uint_as_float(0x7FC00000u);
+        x[(size_t)t * hidden + c] = v;
+        ss += v * v;
+    }
+    float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
+    for (int c = threadIdx.x; c < hidden; c += 256)
+        xn[(size_t)t * hidden + c] = __float2bfloat16_rn(x[(size_t)t * hidden + c] * r * bf(w[c]));
+}
+
+// ---- residual + split reduce + norm --------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) resid_norm_kernel(float *x, const float *partial, int splits,
+                                                         size_t split_stride, int hidden, const __nv_bfloat16 *w,
+                                                         float eps, __nv_bfloat16 *xn) {
+    __shared__ float red[8];
+    const int t = blockIdx.x;
+    float *xr = x + (size_t)t * hidden;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < hidden; c += 256) {
+        float v = xr[c];
+        for (int s = 0; s < splits; ++s) v += partial[s * split_stride + (size_t)t * hidden + c];
+        if (splits) xr[c] = v;
+        ss += v * v;
+    }
+    float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
+    for (int c = threadIdx.x; c < hidden; c += 256)
+        xn[(size_t)t * hidden + c] = __float2bfloat16_rn(xr[c] * r * bf(w[c]));
+}
+
+// ---- q/k norm + RoPE + KV append --------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    return make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+}
+
+// One warp per (token, head row); lane l owns dims 4l..4l+3. Head rows 0..q-1 are q, then kv k rows, then kv v rows.
+__global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(QkvArgs a) {
+    const int warp_global = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int rows = a.q_heads + 2 * a.kv_heads;
+    const int t = warp_global / rows, hr = warp_global % rows;
+    if (t >= a.T) return;
+    const int width = rows * kHeadDim;
+    float4 v = make_float4(0, 0, 0, 0);
+    for (int s = 0; s < a.splits; ++s) {
+        float4 p = *reinterpret_cast<const float4 *>(a.qkv + s * a.split_stride + (size_t)t * width + hr * kHeadDim +
+                                                     4 * lane);
+        v.x += p.x;
+        v.y += p.y;
+        v.z += p.z;
+        v.w += p.w;
+    }
+    const int pos = a.tok_pos[t];
+    const bool is_q = hr < a.q_heads, is_k = !is_q && hr < a.q_heads + a.kv_heads;
+    if (is_q || is_k) {
+        const __nv_bfloat16 *nw = is_q ? a.q_norm : a.k_norm;
+        float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+        float r = rsqrtf(ss / kHeadDim + a.eps);
+        const int d = 4 * lane;
+        float y0 = v.x * r * bf(nw[d]), y1 = v.y * r * bf(nw[d + 1]), y2 = v.z * r * bf(nw[d + 2]),
+              y3 = v.w * r * bf(nw[d + 3]);
+        // NeoX rotate-half: dim i pairs with i + 64, held by lane l ^ 16.
+        float o0 = __shfl_xor_sync(FULL, y0, 16), o1 = __shfl_xor_sync(FULL, y1, 16),
+              o2 = __shfl_xor_sync(FULL, y2, 16), o3 = __shfl_xor_sync(FULL, y3, 16);
+        const int i = 4 * (lane & 15);
+        float4 c = *reinterpret_cast<const float4 *>(a.cos_t + (size_t)pos * 64 + i);
+        float4 s = *reinterpret_cast<const float4 *>(a.sin_t + (size_t)pos * 64 + i);
+        if (lane < 16) {  // y[i] = x[i] c - x[i+64] s
+            v = make_float4(y0 * c.x - o0 * s.x, y1 * c.y - o1 * s.y, y2 * c.z - o2 * s.z, y3 * c.w - o3 * s.w);
+        } else {  // y[i+64] = x[i+64] c + x[i] s
+            v = make_float4(y0 * c.x + o0 * s.x, y1 * c.y + o1 * s.y, y2 * c.z + o2 * s.z, y3 * c.w + o3 * s.w);
+        }
+    }
+    const uint2 packed = pack4(v.x, v.y, v.z, v.w);
+    if (is_q) {
+        *reinterpret_cast<uint2 *>(a.q_out + ((size_t)t * a.q_heads + hr) * kHeadDim + 4 * lane) = packed;
+        return;
+    }
+    const int kvh = is_k ? hr - a.q_heads : hr - a.q_heads - a.kv_heads;
+    const int slot = a.tok_slot[t];
+    const int page = a.kv.pages[(size_t)slot * a.kv.max_pages_per_seq + pos / kPageTokens];
+    __nv_bfloat16 *dst = a.kv.pool + (size_t)page * kv_page_elems(a.kv_heads) +
+                         ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * kPageTokens + pos % kPageTokens) * kHeadDim + 4 * lane;
+    *reinterpret_cast<uint2 *>(dst) = packed;
+    __nv_bfloat16 *contig = is_k ? a.k_out : a.v_out;
+    if (contig) *reinterpret_cast<uint2 *>(contig + ((size_t)t * a.kv_heads + kvh) * kHeadDim + 4 * lane) = packed;
+}
+
+// ---- SwiGLU reduce (decode) ------------------------------------------------------------------------------------
+
+__global__ void swiglu_reduce_kernel(const float *partial, int splits, size_t split_stride, int T, int inter,
+                                     __nv_bfloat16 *act) {
+    size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (size_t)T * inter) return;
+    int t = (int)(e / inter), j = (int)(e % inter);
+    size_t base = (size_t)t * (2 * inter) + (j / 64) * 128 + (j % 64);
+    float g = 0.f, u = 0.f;
+    for (int s = 0; s < splits; ++s) {
+        g += partial[s * split_stride + base];
+        u += partial[s * split_stride + base + 64];
+    }
+    act[e] = __float2bfloat16_rn(g / (1.0f + __expf(-g)) * u);
+}
+
+// ---- argmax -------------------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V, uint32_t *out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int nan_any;
+    const float *row = logits + (size_t)blockIdx.x * V;
+    if (threadIdx.x == 0) nan_any = 0;
+    __syncthreads();
+    float best = -INFINITY;
+    int idx = -1;
+    bool nan = false;
+    for (int c = threadIdx.x; c < V; c += 1024) {
+        float v = row[c];
+        if (isnan(v))
+            nan = true;
+        else if (idx < 0 || v > best) {
+            best = v;
+            idx = c;
+        }
+    }
+    if (nan) nan_any = 1;
+    // warp reduce: larger value, then lower index
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float v2 = __shfl_xor_sync(FULL, best, o);
+        int i2 = __shfl_xor_sync(FULL, idx, o);
+        if (i2 >= 0 && (idx < 0 || v2 > best || (v2 == best && i2 < idx))) {
+            best = v2;
+            idx = i2;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = best;
+        si[threadIdx.x >> 5] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = sv[threadIdx.x];
+        idx = si[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float v2 = __shfl_xor_sync(FULL, best, o);
+            int i2 = __shfl_xor_sync(FULL, idx, o);
+            if (i2 >= 0 && (idx < 0 || v2 > best || (v2 == best && i2 < idx))) {
+                best = v2;
+                idx = i2;
+            }
+        }
+        if (threadIdx.x == 0) out[blockIdx.x] = nan_any ? 0xFFFFFFFFu : (uint32_t)idx;
+    }
+}
+
+__global__ void gather_rows_kernel(const __nv_bfloat16 *src, const int32_t *idx, int cols, __nv_bfloat16 *dst) {
+    const int r = blockIdx.x;
+    const __nv_bfloat16 *s = src + (size_t)idx[r] * cols;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[(size_t)r * cols + c] = s[c];
+}
+
+__global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos) {
+    int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    int slot = slots[b];
+    int p = seq_len[slot];
+    tok_pos[b] = p;
+    seq_len[slot] = p + 1;
+}
+
+// ---- paged split-K decode attention -----------------------------------------------------------------------------
+//
+// CTA = (split, kv head h, batch row b): the pages [split * PPS, ...) of sequence slots[b]. Warp 4 streams each page's
+// K+V block of head h (8 KiB contiguous) into a ring of ST shared-memory stages with cp.async.bulk; consumer warp w
+// (0..3) handles the pages w, w + 4, ... of the split with its own online softmax for the two q heads 2h, 2h + 1:
+//   scores: lane (half = lane / 16, li = lane % 16) reads dims 8 li .. 8 li + 7 of keys 2i + half (16-byte smem
+//           loads, conflict-free), keeps 16 partial dots (8 keys x 2 heads) and a 4-step shuffle reduce-scatter
+//           over the 16 lanes leaves lane li with the full score of key 2 (li / 2) + half for head li % 2;
+//   softmax: log2 domain (scale folded with log2 e), running maximum per head, lane-local sums;
+//   values: lane owns dims 4 lane .. 4 lane + 3 (8-byte smem loads), weights broadcast from shared memory.
+// The four warps' states merge in shared memory and the split's (max, sum, unnormalised output) go to part_*; the
+// combine kernel merges the splits.
+template <int ST>
+__global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
+    constexpr int PAGE_BYTES = 2 * kPageTokens * kHeadDim * 2;  // K + V of one head = 8 KiB
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *stages = smem_raw;
+    float *pbuf = (float *)(stages + ST * PAGE_BYTES);  // [4][32]
+    float *red_acc = pbuf + 4 * 32;                     // [4][2][128]
+    float *red_m = red_acc + 4 * 2 * 128;               // [4][2]
+    float *red_l = red_m + 8;                           // [4][2]
+    uint64_t *full = (uint64_t *)(red_l + 8);
+    uint64_t *empty = full + ST;
+
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int slot = a.slots[b];
+    const int len = a.seq_len[slot];
+    const int npages = (len + kPageTokens - 1) / kPageTokens;
+    const int p0 = split * a.pages_per_split;
+    if (p0 >= npages) return;  // whole CTA, before any barrier
+    const int n = min(npages - p0, a.pages_per_split);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t page_elems = kv_page_elems(a.kv.kv_heads);
+    const int32_t *ptab = a.kv.pages + (size_t)slot * a.kv.max_pages_per_seq;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        ptx::fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == 4) {
+        if (lane == 0) {
+            int j = 0;
+            for (; j < n; ++j) {
+                const int s = j % ST;
+                if (!ptx::mbar_wait(&empty[s], ((j / ST) & 1) ^ 1, a.err, 0x2001)) break;
+                const __nv_bfloat16 *src = a.kv.pool + (size_t)ptab[p0 + j] * page_elems +
+                                           (size_t)h * 2 * kPageTokens * kHeadDim;
+                ptx::mbar_arrive_expect_tx(&full[s], PAGE_BYTES);
+                ptx::bulk_load(stages + s * PAGE_BYTES, src, PAGE_BYTES, &full[s]);
+            }
+            for (int k = j > ST ? j - ST : 0; k < j; ++k) ptx::mbar_wait(&full[k % ST], (k / ST) & 1, a.err, 0x2002);
+        }
+    } else {
+        const int half = lane >> 4, li = lane & 15;
+        float q0[8], q1[8];
+        {
+            const uint4 r0 = *reinterpret_cast<const uint4 *>(a.q + ((size_t)b * a.q_heads + 2 * h) * kHeadDim + 8 * li);
+            const uint4 r1 =
+                *reinterpret_cast<const uint4 *>(a.q + ((size_t)b * a.q_heads + 2 * h + 1) * kHeadDim + 8 * li);
+            const uint32_t w0[4] = {r0.x, r0.y, r0.z, r0.w}, w1[4] = {r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                q0[2 * i] = __uint_as_float(w0[i] << 16) * a.scale_log2;
+                q0[2 * i + 1] = __uint_as_float(w0[i] & 0xFFFF0000u) * a.scale_log2;
+                q1[2 * i] = __uint_as_float(w1[i] << 16) * a.scale_log2;
+                q1[2 * i + 1] = __uint_as_float(w1[i] & 0xFFFF0000u) * a.scale_log2;
+            }
+        }
+        float m_run = -INFINITY, l_lane = 0.f;
+        float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
+        float *pw = pbuf + warp * 32;
+        for (int j = warp; j < n; j += 4) {
+            const int s = j % ST;
+            if (!ptx::mbar_wait(&full[s], (j / ST) & 1, a.err, 0x2003)) break;
+            const uint8_t *kb = stages + s * PAGE_BYTES;
+            const uint8_t *vb = kb + PAGE_BYTES / 2;
+            const int tok0 = (p0 + j) * kPageTokens;
+            const int valid = min(kPageTokens, len - tok0);
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint4 kr = *reinterpret_cast<const uint4 *>(kb + (2 * i + half) * 256 + li * 16);
+                const uint32_t w[4] = {kr.x, kr.y, kr.z, kr.w};
+                float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float ka = __uint_as_float(w[e] << 16), kb2 = __uint_as_float(w[e] & 0xFFFF0000u);
+                    d0 = fmaf(q0[2 * e], ka, d0);
+                    d0 = fmaf(q0[2 * e + 1], kb2, d0);
+                    d1 = fmaf(q1[2 * e], ka, d1);
+                    d1 = fmaf(q1[2 * e + 1], kb2, d1);
+                }
+                v[2 * i] = d0;
+                v[2 * i + 1] = d1;
+            }
+            // reduce-scatter over the 16 lanes of this half: lane li ends with value index li
+#pragma unroll
+            for (int step = 0; step < 4; ++step) {
+                const int m = 8 >> step, cnt = 16 >> step;
+                const bool upper = (li & m) != 0;
+#pragma unroll
+                for (int i = 0; i < cnt / 2; ++i) {
+                    const float send = upper ? v[i] : v[i + cnt / 2];
+                    const float keep = upper ? v[i + cnt / 2] : v[i];
+                    v[i] = keep + __shfl_xor_sync(FULL, send, m);
+                }
+            }
+            const int key = 2 * (li >> 1) + half;
+            float sc = key < valid ? v[0] : -INFINITY;
+            float pm = sc;
+            pm = fmaxf(pm, __shfl_xor_sync(FULL, pm, 2));
+            pm = fmaxf(pm, __shfl_xor_sync(FULL, pm, 4));
+            pm = fmaxf(pm, __shfl_xor_sync(FULL, pm, 8));
+            pm = fmaxf(pm, __shfl_xor_sync(FULL, pm, 16));
+            const float m_new = fmaxf(m_run, pm);
+            const float alpha = exp2f(m_run - m_new);
+            const float p = exp2f(sc - m_new);
+            m_run = m_new;
+            l_lane = l_lane * alpha + p;
+            pw[key * 2 + (li & 1)] = p;
+            const float al0 = __shfl_sync(FULL, alpha, 0), al1 = __shfl_sync(FULL, alpha, 1);
+            __syncwarp();
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                acc0[e] *= al0;
+                acc1[e] *= al1;
+            }
+            for (int t = 0; t < valid; ++t) {
+                const uint2 vr = *reinterpret_cast<const uint2 *>(vb + t * 256 + lane * 8);
+                const float2 pp = *reinterpret_cast<const float2 *>(pw + 2 * t);
+                const float va = __uint_as_float(vr.x << 16), vb2 = __uint_as_float(vr.x & 0xFFFF0000u),
+                            vc = __uint_as_float(vr.y << 16), vd = __uint_as_float(vr.y & 0xFFFF0000u);
+                acc0[0] = fmaf(pp.x, va, acc0[0]);
+                acc0[1] = fmaf(pp.x, vb2, acc0[1]);
+                acc0[2] = fmaf(pp.x, vc, acc0[2]);
+                acc0[3] = fmaf(pp.x, vd, acc0[3]);
+                acc1[0] = fmaf(pp.y, va, acc1[0]);
+                acc1[1] = fmaf(pp.y, vb2, acc1[1]);
+                acc1[2] = fmaf(pp.y, vc, acc1[2]);
+                acc1[3] = fmaf(pp.y, vd, acc1[3]);
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&empty[s]);
+        }
+        // per-head totals of this warp
+        float l = l_lane;
+        l += __shfl_xor_sync(FULL, l, 2);
+        l += __shfl_xor_sync(FULL, l, 4);
+        l += __shfl_xor_sync(FULL, l, 8);
+        l += __shfl_xor_sync(FULL, l, 16);
+        if (lane < 2) {
+            red_m[warp * 2 + lane] = m_run;
+            red_l[warp * 2 + lane] = l;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            red_acc[(warp * 2 + 0) * 128 + 4 * lane + e] = acc0[e];
+            red_acc[(warp * 2 + 1) * 128 + 4 * lane + e] = acc1[e];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int d = threadIdx.x;
+        const size_t base = ((size_t)b * a.kv.kv_heads + h) * a.max_splits + split;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) M = fmaxf(M, red_m[w * 2 + hh]);
+            float o = 0.f, l = 0.f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const float f = red_m[w * 2 + hh] == -INFINITY ? 0.f : exp2f(red_m[w * 2 + hh] - M);
+                o += f * red_acc[(w * 2 + hh) * 128 + d];
+                l += f * red_l[w * 2 + hh];
+            }
+            a.part_o[(base * 2 + hh) * 128 + d] = o;
+            if (d == 0) {
+                a.part_ml[(base * 2 + hh) * 2 + 0] = M;
+                a.part_ml[(base * 2 + hh) * 2 + 1] = l;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
+    const int b = blockIdx.x, qh = blockIdx.y, d = threadIdx.x;
+    const int h = qh / 2, hh = qh % 2;
+    const int len = a.seq_len[a.slots[b]];
+    const int npages = (len + kPageTokens - 1) / kPageTokens;
+    const int nsplit = (npages + a.pages_per_split - 1) / a.pages_per_split;
+    const size_t base = ((size_t)b * a.kv.kv_heads + h) * a.max_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, a.part_ml[((base + s) * 2 + hh) * 2]);
+    float o = 0.f, l = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+        const float m = a.part_ml[((base + s) * 2 + hh) * 2];
+        const float f = m == -INFINITY ? 0.f : exp2f(m - M);
+        o += f * a.part_o[((base + s) * 2 + hh) * 128 + d];
+        l += f * a.part_ml[((base + s) * 2 + hh) * 2 + 1];
+    }
+    a.out[((size_t)b * a.q_heads + qh) * kHeadDim + d] = __float2bfloat16_rn(o / l);
+}
+
+}  // namespace
+
+cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
+                              const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st) {
+    embed_norm_kernel<<<T, 256, 0, st>>>(ids, embed, hidden, vocab, w, eps, x, xn);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
+                              const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st) {
+    resid_norm_kernel<<<T, 256, 0, st>>>(x, partial, splits, split_stride, hidden, w, eps, xn);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qk_norm_rope_kv(const QkvArgs &a, cudaStream_t st) {
+    const int warps = a.T * (a.q_heads + 2 * a.kv_heads);
+    qk_norm_rope_kv_kernel<<<(warps + 7) / 8, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_reduce(const float *partial, int splits, size_t split_stride, int T, int inter,
+                                 __nv_bfloat16 *act, cudaStream_t st) {
+    size_t n = (size_t)T * inter;
+    swiglu_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partial, splits, split_stride, T, inter, act);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st) {
+    argmax_kernel<<<R, 1024, 0, st>>>(logits, V, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const __nv_bfloat16 *src, const int32_t *idx, int R, int cols, __nv_bfloat16 *dst,
+                               cudaStream_t st) {
+    gather_rows_kernel<<<R, 256, 0, st>>>(src, idx, cols, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos, cudaStream_t st) {
+    advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(slots, B, seq_len, tok_pos);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
+    constexpr int ST = 8;
+    const size_t smem = ST * 8192 + (4 * 32 + 4 * 2 * 128 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        configured[dev & 63] = true;
+    }
+    dim3 grid(a.max_splits, a.kv.kv_heads, a.B);
+    decode_attn_kernel<ST><<<grid, 160, smem, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    decode_combine_kernel<<<dim3(a.B, a.q_heads), 128, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace lrm

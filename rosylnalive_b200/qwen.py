@@ -1,0 +1,162 @@
+"""The bf16 Qwen3 engine (liblrmcuda.so lrm_qwen_*), the fast path of the forward.
+
+The reference plans this layer as Lrm.Gpu.Exec / Lrm.Models.Qwen (docs/dev-plan.md, "GpuForwardOps", "Greedy.run");
+both are placeholders there. QwenEngine runs the same schedule as tests/Lrm.Tensor.Tests/TinyModel.fs:144-236 --
+one prefill, then single-token greedy steps, argmax of the last row -- for many sequences at once, with bf16
+weights/activations, an fp32 residual stream and a paged bf16 KV cache.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import native as N
+from .executor import QwenConfig, weight_shapes
+
+P, I32, U32, U64, F32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
+
+
+class QwenConfigC(ctypes.Structure):
+    _fields_ = [("layers", I32), ("hidden", I32), ("q_heads", I32), ("kv_heads", I32), ("head_dim", I32),
+                ("intermediate", I32), ("vocab", I32), ("eps", F32), ("max_pos", I32), ("max_seqs", I32),
+                ("kv_pages", I32), ("max_tokens", I32), ("max_batch", I32)]
+
+
+PI32, PU32, PF32, PU16 = (ctypes.POINTER(t) for t in (I32, U32, F32, ctypes.c_uint16))
+
+N.extra_signatures({
+    "lrm_qwen_create": [I32, ctypes.POINTER(QwenConfigC), ctypes.POINTER(P)],
+    "lrm_qwen_destroy": [P],
+    "lrm_qwen_set_weight": [P, ctypes.c_char_p, PU16, U64],
+    "lrm_qwen_set_rope": [P, PF32, PF32, I32, I32],
+    "lrm_qwen_reset_seq": [P, I32],
+    "lrm_qwen_reserve": [P, I32, I32],
+    "lrm_qwen_prefill": [P, I32, PI32, PI32, PU32, PU32, PF32],
+    "lrm_qwen_decode": [P, I32, PI32, PU32, PU32, PF32],
+    "lrm_qwen_decode_graph": [P, I32, PI32, PU32],
+    "lrm_qwen_decode_replay": [P, I32],
+    "lrm_qwen_last_ids": [P, PU32],
+    "lrm_qwen_sync": [P],
+    "lrm_qwen_stream": [P, ctypes.POINTER(P)],
+    "lrm_qwen_seq_len": [P, I32, PI32],
+})
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(ctypes.POINTER(t))
+
+
+class QwenEngine:
+    """One device's Qwen3 engine. `weights` maps HF names to bf16 bit arrays (uint16)."""
+
+    def __init__(self, cfg: QwenConfig, weights: dict, rope_cos: np.ndarray, rope_sin: np.ndarray, device: int = 0,
+                 max_seqs: int = 64, kv_pages: int | None = None, max_tokens: int = 4096, max_batch: int = 64,
+                 max_pos: int | None = None):
+        self.cfg = cfg
+        max_pos = max_pos or cfg.max_pos
+        pages_per_seq = (max_pos + 15) // 16
+        kv_pages = kv_pages or max_seqs * pages_per_seq
+        c = QwenConfigC(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate, cfg.vocab,
+                        cfg.eps, max_pos, max_seqs, kv_pages, max_tokens, max_batch)
+        h = ctypes.c_void_p()
+        N.check(N.lib().lrm_qwen_create(device, ctypes.byref(c), ctypes.byref(h)), None, "lrm_qwen_create")
+        self._h = h
+        self.max_seqs, self.max_tokens, self.max_batch, self.max_pos = max_seqs, max_tokens, max_batch, max_pos
+        for name, shape in weight_shapes(cfg).items():
+            w = np.ascontiguousarray(weights[name], np.uint16)
+            if w.shape != tuple(shape):
+                raise ValueError(f"{name} is {w.shape}, expected {shape}")
+            self._check(N.lib().lrm_qwen_set_weight(self._h, name.encode(), _p(w, ctypes.c_uint16), w.size),
+                        "set_weight")
+        cos = np.ascontiguousarray(rope_cos[:max_pos], np.float32)
+        sin = np.ascontiguousarray(rope_sin[:max_pos], np.float32)
+        if cos.shape[0] < max_pos:
+            raise ValueError("the RoPE table has fewer rows than max_pos")
+        self._check(N.lib().lrm_qwen_set_rope(self._h, _p(cos, F32), _p(sin, F32), cos.shape[0], cos.shape[1]),
+                    "set_rope")
+
+    def _check(self, status, what):
+        if status != N.LRM_OK:
+            N.check(status, None, what)
+
+    def close(self):
+        if self._h:
+            N.lib().lrm_qwen_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        self._check(N.lib().lrm_qwen_stream(self._h, ctypes.byref(s)), "stream")
+        return s.value or 0
+
+    def prefill(self, slots, prompts, want_logits=False):
+        """Fresh prefill of prompts[i] into slots[i]; returns (next ids [n], last-row logits [n, vocab] or None)."""
+        slots = np.ascontiguousarray(slots, np.int32)
+        lens = np.array([len(p) for p in prompts], np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]), np.uint32)
+        nxt = np.empty(len(prompts), np.uint32)
+        logits = np.empty((len(prompts), self.cfg.vocab), np.float32) if want_logits else None
+        self._check(N.lib().lrm_qwen_prefill(self._h, len(prompts), _p(slots, I32), _p(lens, I32), _p(ids, U32),
+                                             _p(nxt, U32), _p(logits, F32) if want_logits else None), "prefill")
+        return nxt, logits
+
+    def decode(self, slots, ids, want_logits=False):
+        slots = np.ascontiguousarray(slots, np.int32)
+        ids = np.ascontiguousarray(ids, np.uint32)
+        nxt = np.empty(len(slots), np.uint32)
+        logits = np.empty((len(slots), self.cfg.vocab), np.float32) if want_logits else None
+        self._check(N.lib().lrm_qwen_decode(self._h, len(slots), _p(slots, I32), _p(ids, U32), _p(nxt, U32),
+                                            _p(logits, F32) if want_logits else None), "decode")
+        return nxt, logits
+
+    def capture(self, slots, first_ids=None):
+        """Captures the device-resident decode step for `slots` (inputs: the previous step's outputs)."""
+        slots = np.ascontiguousarray(slots, np.int32)
+        fid = None if first_ids is None else np.ascontiguousarray(first_ids, np.uint32)
+        self._check(N.lib().lrm_qwen_decode_graph(self._h, len(slots), _p(slots, I32),
+                                                  _p(fid, U32) if fid is not None else None), "decode_graph")
+        self._graph_batch = len(slots)
+
+    def replay(self, steps: int):
+        self._check(N.lib().lrm_qwen_decode_replay(self._h, steps), "decode_replay")
+
+    def last_ids(self):
+        out = np.empty(self._graph_batch, np.uint32)
+        self._check(N.lib().lrm_qwen_last_ids(self._h, _p(out, U32)), "last_ids")
+        return out
+
+    def sync(self):
+        self._check(N.lib().lrm_qwen_sync(self._h), "sync")
+
+    def reserve(self, slot: int, tokens: int):
+        self._check(N.lib().lrm_qwen_reserve(self._h, slot, tokens), "reserve")
+
+    def seq_len(self, slot: int) -> int:
+        v = ctypes.c_int32()
+        self._check(N.lib().lrm_qwen_seq_len(self._h, slot, ctypes.byref(v)), "seq_len")
+        return v.value
+
+    def greedy(self, prompts, steps: int, slots=None, want_logits=False):
+        """The canonical greedy schedule for each prompt: prefill, then steps - 1 single-token decode steps.
+        Returns ids [n, steps] (and logits [n, steps, vocab] when asked)."""
+        n = len(prompts)
+        slots = np.arange(n, dtype=np.int32) if slots is None else np.asarray(slots, np.int32)
+        nxt, lg = self.prefill(slots, prompts, want_logits)
+        ids, logs = [nxt.copy()], [lg]
+        for _ in range(1, steps):
+            nxt, lg = self.decode(slots, nxt, want_logits)
+            ids.append(nxt.copy())
+            logs.append(lg)
+        ids = np.stack(ids, 1).astype(np.int64)
+        if want_logits:
+            return ids, np.stack(logs, 1)
+        return ids
