@@ -1,0 +1,379 @@
+"""Benchmark of the Qwen3 decoder forward on B200 (BASELINE.json metric: Qwen3-0.6B-shape tok/s, prefill and decode
+b=64, at 1/2/4/8 GPUs, % HBM roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: one process per GPU)
+
+Headline (value): BASELINE config 5 -- Qwen3-0.6B architecture, random N(0, 0.02) bf16 weights, greedy decode of 64
+sequences per GPU, each with a 4096-token paged KV cache (16-token pages) prefilled from uniform-random ids through
+the engine's own prefill; one step = one decode step of the 64 sequences (64 tokens per GPU). Sequences are
+independent, so N GPUs run N x 64 (weak scaling, no collective on the hot path). The timed region replays the
+captured decode step K times with every input resident on the device; e2e repeats the same K steps through the
+public host API (ids copied in from pinned memory and next ids copied out every step). The KV cache (32 GB) is far
+larger than L2, so no flush is needed between steps.
+
+Also reported: BASELINE config 4 prefill (16 x 2048-token prompts per job, split over the GPUs), the decode-attention
+kernel's HBM roofline (timed with CUDA events recorded inside the replayed step), clocks sampled during the timed
+region, and the CPU reference (the oracle port) timed on a bounded sample on this host.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Qwen3-0.6B-shape tok/s (prefill, decode b=64) at 1/2/4/8 B200; % HBM roofline"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=248)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    p.add_argument("--context", type=int, default=4096, help="prefilled KV tokens per sequence")
+    p.add_argument("--no-prefill-bench", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample, seconds")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS if k in d}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self):
+        import datetime
+
+        import torch
+
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device(f"cuda:{self.local}"))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], device=f"cuda:{self.local}", dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.gpu_ids = gpu_ids
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i",
+                 ",".join(self.gpu_ids)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [[x.strip() for x in ln.split(",")] for ln in out.splitlines() if ln.strip()]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        load = [s for s in sm if s > 0.5 * (max(sm) if sm else 0)]
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---- the CPU reference (the oracle port; the reference's F# CPU path cannot be built here) ----------------------
+
+
+def cpu_decode_sample(weights, cfg, context, seconds, max_steps=None):
+    """Times CPU-reference decode steps of one sequence at `context` cached tokens (fp32 cache filled with random
+    values: the cost of a step does not depend on them). Returns (tok/s, steps, seconds, threads)."""
+    from oracle import oracle as O
+    from rosylnalive_b200 import rope as R
+
+    steps_cap = max_steps or 10 ** 6
+    max_pos = context + min(steps_cap, 4096) + 1
+    cos, sin = R.t_spec(R.QWEN3_INV_FREQ_BITS, max_pos)
+    oc = O.Config(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate, cfg.vocab, cfg.eps,
+                  max_pos)
+    m = O.Model.from_hf(oc, weights, cos, sin)
+    cache = O.Cache.new(oc, "f32", max_pos)
+    g = np.random.default_rng(7)
+    for arr in cache.keys + cache.values:
+        arr[:context] = g.standard_normal((context, arr.shape[1]), dtype=np.float32)
+    tok = 1
+    t0 = time.perf_counter()
+    n = 0
+    while n < steps_cap and n + context < max_pos - 1:
+        logits = O.forward(m, cache, context + n, [tok], "f32", logits_rows="last")
+        tok = int(O.argmax_rows(logits, "f32")[0])
+        n += 1
+        if max_steps is None and time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return n / dt, n, dt, O.THREADS
+
+
+def run_reference(args, dist):
+    from rosylnalive_b200 import synthetic as S
+
+    if dist.rank != 0:
+        return
+    cfg = S.QWEN3_0_6B
+    weights = S.random_weights(cfg, seed=0)
+    cpu_decode_sample(weights, cfg, args.context, 0, max_steps=max(1, args.warmup))
+    tps, n, dt, threads = cpu_decode_sample(weights, cfg, args.context, 0, max_steps=max(1, args.steps))
+    sample = (f"{n} CPU-reference decode steps of 1 sequence at {args.context} cached tokens (fp32 cache), "
+              f"Qwen3-0.6B shape, {threads} threads; the config-5 step is 64 such sequences")
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": n, "warmup": args.warmup, "ms_per_step": 1000 * dt / n, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config5-sample: Qwen3-0.6B greedy decode, CPU reference, 1 sequence",
+                       "seq_len": args.context},
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm -------------------------------------------------------------------------------------------------
+
+
+def run_ours(args, dist):
+    import torch
+
+    from rosylnalive_b200 import qwen as Qw
+    from rosylnalive_b200 import rope as R
+    from rosylnalive_b200 import synthetic as S
+
+    pk, pk_kind = peaks()
+    cfg = S.QWEN3_0_6B
+    B, ctx, K, W = args.batch, args.context, args.steps, args.warmup
+    weights = S.random_weights(cfg, seed=0)
+    max_pos = (ctx + W + K + 16 + 15) // 16 * 16
+    cos, sin = R.t_spec(R.QWEN3_INV_FREQ_BITS, max_pos)
+    chunk = max(1, min(B, 32768 // ctx))
+    eng = Qw.QwenEngine(cfg, weights, cos, sin, device=dist.local, max_seqs=max(B, 16), max_tokens=32768,
+                        max_batch=B, max_pos=max_pos)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    slots = np.arange(B, dtype=np.int32)
+
+    # KV prefill from random ids (setup, not timed).
+    prompts = S.random_prompts(cfg.vocab, B, ctx, seed=1000 + dist.rank)
+    first = []
+    for i in range(0, B, chunk):
+        nxt, _ = eng.prefill(slots[i:i + chunk], list(prompts[i:i + chunk]))
+        first.extend(nxt.tolist())
+    eng.capture(slots, np.array(first, np.uint32))
+    launches_per_step = eng.graph_kernels()
+    eng.replay(W)
+    eng.sync()
+    start_len = ctx + W
+    ids_at_start = eng.last_ids()
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record()
+            fn()
+            e1.record()
+        e1.synchronize()
+        torch.cuda.synchronize()
+        dist.barrier()
+        return dist.max(e0.elapsed_time(e1))
+
+    gpu_ids = [torch.cuda.get_device_properties(i).uuid for i in range(torch.cuda.device_count())]
+    sampler = ClockSampler([f"GPU-{u}" if not str(u).startswith("GPU-") else str(u) for u in gpu_ids]
+                           if dist.rank == 0 else [])
+    if dist.rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    ms = timed(lambda: eng.replay(K))
+    clocks = sampler.stop() if dist.rank == 0 else None
+    value = B * dist.world * K / (ms / 1000.0)
+
+    # e2e: the same K steps (rewound to the same positions) through the public host API.
+    for s in slots:
+        eng.truncate(int(s), start_len)
+    cur = ids_at_start.copy()
+
+    def e2e_steps():
+        nonlocal cur
+        for _ in range(K):
+            cur, _ = eng.decode(slots, cur)
+
+    ms_e2e = timed(e2e_steps)
+    e2e_value = B * dist.world * K / (ms_e2e / 1000.0)
+
+    # Roofline of the dominant kernel (decode attention): events around each layer's launch inside the step.
+    for s in slots:
+        eng.truncate(int(s), start_len)
+    eng.capture(slots, ids_at_start, time_attention=True)
+    R_steps = min(K, 32)
+    att_ms, att_bytes = [], []
+    kvh, hd = cfg.kv_heads, cfg.head_dim
+    for i in range(R_steps):
+        eng.replay(1)
+        per_layer = eng.attention_ms()
+        keys = start_len + i + 1
+        att_ms.extend(per_layer.tolist())
+        # algorithmic bytes of one launch: K and V of every cached key (bf16) + q in + out (bf16)
+        att_bytes.extend([B * keys * kvh * hd * 2 * 2 + 2 * B * cfg.heads * hd * 2] * len(per_layer))
+    att_avg_ms = float(np.mean(att_ms))
+    att_bytes_avg = float(np.mean(att_bytes))
+    achieved = att_bytes_avg / (att_avg_ms / 1000.0) / 1e9
+    traffic = profile_traffic("decode_attention", att_bytes_avg)
+    roofline = {"kernel": "decode_attn_kernel + decode_combine_kernel", "bound": "hbm", "achieved": achieved,
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                "peak_source": f"{pk_kind} hbm_gbs", "algorithmic_bytes_per_launch": att_bytes_avg,
+                "avg_launch_ms": att_avg_ms, "launches_timed": len(att_ms),
+                "share_of_step": float(np.sum(att_ms) / R_steps) / (ms / K)}
+    # Whole-step HBM roofline: algorithmic bytes of one decode step (weights once, KV of every key, logits).
+    step_bytes = (weights_bytes(cfg) + B * (start_len + K / 2) * cfg.layers * kvh * hd * 2 * 2
+                  + B * cfg.vocab * 4)
+    step_roof = {"algorithmic_bytes_per_step": step_bytes,
+                 "achieved_gbs": step_bytes / (ms / K / 1000.0) / 1e9,
+                 "frac": step_bytes / (ms / K / 1000.0) / 1e9 / pk["hbm_gbs"]}
+
+    prefill = None
+    if not args.no_prefill_bench:
+        prefill = prefill_bench(eng, cfg, dist, pk, stream, timed)
+    eng.close()
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        tps, n, dt, threads = cpu_decode_sample(weights, cfg, ctx, args.cpu_seconds)
+        cpu = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n} CPU-reference (oracle port) decode steps of 1 sequence at {ctx} cached tokens, "
+                         f"{dt:.1f} s on {threads} threads"}
+
+    if dist.rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": K, "warmup": W,
+                "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "config5: Qwen3-0.6B bf16 greedy decode, 64 seqs/GPU, 4096-token paged KV "
+                                       "(16-token pages), random-init weights N(0,0.02), random prompt ids",
+                           "model": "Qwen3-0.6B architecture", "global_batch": B * dist.world, "seq_len": ctx,
+                           "parallelism": f"dp{dist.world} (independent sequences per GPU, no collective)",
+                           "l2": "inputs larger than L2 (32 GB KV cache), no flush"},
+                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
+                "gpu_launches": launches_per_step * K, "roofline": roofline, "step_roofline": step_roof,
+                "prefill": prefill, "cpu_baseline": cpu, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
+def weights_bytes(cfg) -> int:
+    from rosylnalive_b200.executor import weight_shapes
+
+    return int(sum(np.prod(s) for s in weight_shapes(cfg).values()) * 2)
+
+
+def profile_traffic(kernel: str, algorithmic_bytes: float):
+    """DRAM bytes per launch from the committed ncu summary of the kernel (profiles/<kernel>_traffic.json: bytes
+    per algorithmic byte, measured on a smaller case), scaled to this launch; None when no summary exists."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    return float(d["dram_bytes_per_algorithmic_byte"]) * algorithmic_bytes
+
+
+def prefill_bench(eng, cfg, dist, pk, stream, timed):
+    """16 x 2048-token prompts per job, 16 / N per GPU (strong scaling)."""
+    from rosylnalive_b200 import synthetic as S
+
+    nseq = max(1, 16 // dist.world)
+    L = 2048
+    prompts = list(S.random_prompts(cfg.vocab, nseq, L, seed=2000 + dist.rank))
+    slots = np.arange(nseq, dtype=np.int32)
+    for _ in range(2):
+        eng.prefill(slots, prompts)
+    reps = 3
+    ms = timed(lambda: [eng.prefill(slots, prompts) for _ in range(reps)]) / reps
+    tokens_job = nseq * dist.world * L
+    # algorithmic FLOPs per GPU (the reference's OpCost conventions): GEMMs 2 * params * tokens, attention
+    # 4 * hd * (causal pairs) per head and layer, lm_head on the last rows
+    from rosylnalive_b200.executor import weight_shapes
+
+    layer_params = sum(np.prod(s) for n, s in weight_shapes(cfg).items() if ".layers." in n and s.__len__() == 2)
+    gemm_flops = 2 * layer_params * nseq * L
+    attn_flops = cfg.layers * cfg.heads * nseq * (L * (L + 1) / 2) * (4 * cfg.head_dim)
+    head_flops = 2 * cfg.vocab * cfg.hidden * nseq
+    flops = gemm_flops + attn_flops + head_flops
+    achieved = flops / (ms / 1000.0) / 1e12
+    return {"value": tokens_job / (ms / 1000.0), "unit": "tok/s", "ms_per_prefill": ms,
+            "workload": f"config4: {nseq * dist.world} x {L}-token prompts, {nseq} per GPU (strong scaling)",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / pk["bf16_tflops"], "flops_per_gpu": flops,
+                         "note": "whole prefill (GEMMs + attention + norms) against the bf16 GEMM peak"}}
+
+
+def main():
+    args = parse()
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+        return
+    dist.init()
+    try:
+        run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -239,8 +239,23 @@ lrm_status lrm_qwen_prefill(lrm_qwen q, int32_t nseq, const int32_t *slots, cons
 lrm_status lrm_qwen_decode(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *ids, uint32_t *next_ids,
                            float *logits);
 
-/* Captures the decode step for `slots` as a CUDA graph whose input ids are the previous step's outputs. */
-lrm_status lrm_qwen_decode_graph(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *first_ids);
+/* Captures the decode step for `slots` as a CUDA graph whose input ids are the previous step's outputs. With
+ * LRM_QWEN_GRAPH_TIME_ATTENTION in flags, the graph also records CUDA events around every layer's decode attention,
+ * read back by lrm_qwen_attention_ms after a replay. */
+#define LRM_QWEN_GRAPH_TIME_ATTENTION 0x1u
+lrm_status lrm_qwen_decode_graph(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *first_ids,
+                                 uint32_t flags);
+
+/* Kernel launches in one replay of the captured decode step (its kernel nodes). */
+lrm_status lrm_qwen_graph_kernels(lrm_qwen q, int32_t *kernels);
+
+/* After a replay of a graph captured with LRM_QWEN_GRAPH_TIME_ATTENTION: the decode-attention time of each layer
+ * (ms, [layers]) in that replay. Waits for the stream. */
+lrm_status lrm_qwen_attention_ms(lrm_qwen q, float *ms);
+
+/* Sets a slot's length back to `len` (<= its current length), keeping its pages: later steps overwrite the cache
+ * from position len on. */
+lrm_status lrm_qwen_truncate(lrm_qwen q, int32_t slot, int32_t len);
 
 /* Replays the captured step `steps` times on the engine's stream (asynchronous; lrm_qwen_sync waits). */
 lrm_status lrm_qwen_decode_replay(lrm_qwen q, int32_t steps);

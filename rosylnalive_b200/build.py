@@ -105,7 +105,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             for k, v in sorted(logs.items()):
                 f.write(f"==== {k}\n{v}\n")
     if jobs or not os.path.exists(LIB):
-        cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH + ["-lcuda"]
+        cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -91,6 +91,9 @@ struct lrm_qwen_s {
     // decode graph
     cudaGraphExec_t graph = nullptr;
     int graph_batch = 0;
+    int graph_kernels = 0;
+    bool graph_timed = false;
+    std::vector<cudaEvent_t> attn_ev;  // 2 per layer, recorded inside a timed graph
     std::vector<int32_t> graph_slots;
     // staging
     uint32_t *h_pinned = nullptr;
@@ -158,7 +161,7 @@ static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, i
 #define KTRY(Q, call, what) QTRY(Q, call, what)
 
 // One decode step over device-resident ids/slots (Q->ids[0..B), Q->d_slots) -> Q->next; logits in Q->partial.
-static lrm_status decode_step(lrm_qwen Q, int B) {
+static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
     const lrm_qwen_config &c = Q->c;
     cudaStream_t st = Q->stream;
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
@@ -207,7 +210,9 @@ static lrm_status decode_step(lrm_qwen Q, int B) {
         da.part_ml = Q->part_ml;
         da.out = Q->attn;
         da.err = Q->err;
+        if (timed) KTRY(Q, cudaEventRecordWithFlags(Q->attn_ev[2 * l], st, cudaEventRecordExternal), "event");
         KTRY(Q, launch_decode_attention(da, st), "decode_attention");
+        if (timed) KTRY(Q, cudaEventRecordWithFlags(Q->attn_ev[2 * l + 1], st, cudaEventRecordExternal), "event");
         LTRY(gemm(Q, L.w_o, Q->attn, H, B, qh * kHeadDim, EPI_PARTIAL, 64, s_o, Q->partial, H, nullptr, 0,
                   (size_t)B * H));
         KTRY(Q, launch_resid_norm(Q->x, Q->partial, s_o, (size_t)B * H, B, H, L.post_norm, c.eps, Q->xn, st),
@@ -361,6 +366,7 @@ lrm_status lrm_qwen_destroy(lrm_qwen Q) {
     cudaSetDevice(Q->device);
     cudaStreamSynchronize(Q->stream);
     if (Q->graph) cudaGraphExecDestroy(Q->graph);
+    for (auto e : Q->attn_ev) cudaEventDestroy(e);
     cudaFree(Q->wmem);
     cudaFree(Q->cos_t);
     cudaFree(Q->sin_t);
@@ -598,8 +604,14 @@ lrm_status lrm_qwen_decode(lrm_qwen Q, int32_t batch, const int32_t *slots, cons
     return LRM_OK;
 }
 
-lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots, const uint32_t *first_ids) {
+lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots, const uint32_t *first_ids,
+                                 uint32_t flags) {
     LTRY(check_ready(Q));
+    const bool timed = flags & LRM_QWEN_GRAPH_TIME_ATTENTION;
+    if (timed && Q->attn_ev.empty()) {
+        Q->attn_ev.resize(2 * Q->c.layers);
+        for (auto &e : Q->attn_ev) QTRY(Q, cudaEventCreate(&e), "event");
+    }
     LTRY(set_slots(Q, batch, slots));
     if (first_ids) {
         memcpy(Q->h_pinned, first_ids, 4 * (size_t)batch);
@@ -612,7 +624,7 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
     }
     cudaGraph_t g;
     QTRY(Q, cudaStreamBeginCapture(Q->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-    lrm_status s = decode_step(Q, batch);
+    lrm_status s = decode_step(Q, batch, timed);
     if (s == LRM_OK) {
         cudaError_t e = cudaMemcpyAsync(Q->ids, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToDevice, Q->stream);
         if (e != cudaSuccess) s = qcuda(Q, e, "feedback copy");
@@ -620,9 +632,20 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
     cudaError_t e = cudaStreamEndCapture(Q->stream, &g);
     if (s != LRM_OK) return s;
     QTRY(Q, e, "end capture");
+    size_t nodes = 0;
+    cudaGraphGetNodes(g, nullptr, &nodes);
+    std::vector<cudaGraphNode_t> list(nodes);
+    cudaGraphGetNodes(g, list.data(), &nodes);
+    int kernels = 0;
+    for (auto n : list) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(n, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+    }
     e = cudaGraphInstantiate(&Q->graph, g, 0);
     cudaGraphDestroy(g);
     QTRY(Q, e, "graph instantiate");
+    Q->graph_kernels = kernels;
+    Q->graph_timed = timed;
     Q->graph_batch = batch;
     Q->graph_slots.assign(slots, slots + batch);
     return LRM_OK;
@@ -643,6 +666,35 @@ lrm_status lrm_qwen_last_ids(lrm_qwen Q, uint32_t *ids) {
     LTRY(sync_check(Q));
     QTRY(Q, cudaMemcpy(ids, Q->next, 4 * (size_t)(Q->graph_batch ? Q->graph_batch : 1), cudaMemcpyDeviceToHost),
          "ids");
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_graph_kernels(lrm_qwen Q, int32_t *kernels) {
+    if (!Q || !kernels) return LRM_ERR_ARGUMENT;
+    if (!Q->graph) return qfail(Q, LRM_ERR_STATE, "no decode graph captured");
+    *kernels = Q->graph_kernels;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_attention_ms(lrm_qwen Q, float *ms) {
+    if (!Q || !ms) return LRM_ERR_ARGUMENT;
+    if (!Q->graph || !Q->graph_timed) return qfail(Q, LRM_ERR_STATE, "no timed decode graph captured");
+    cudaSetDevice(Q->device);
+    LTRY(sync_check(Q));
+    for (int l = 0; l < Q->c.layers; ++l)
+        QTRY(Q, cudaEventElapsedTime(&ms[l], Q->attn_ev[2 * l], Q->attn_ev[2 * l + 1]), "event time");
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_truncate(lrm_qwen Q, int32_t slot, int32_t len) {
+    if (!Q || slot < 0 || slot >= Q->c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "slot out of range");
+    cudaSetDevice(Q->device);
+    LTRY(sync_check(Q));
+    int32_t cur = 0;
+    QTRY(Q, cudaMemcpy(&cur, Q->d_seq_len + slot, 4, cudaMemcpyDeviceToHost), "seq_len");
+    if (len < 0 || len > cur) return qfail(Q, LRM_ERR_ARGUMENT, "truncate can only shorten a sequence");
+    QTRY(Q, cudaMemcpy(Q->d_seq_len + slot, &len, 4, cudaMemcpyHostToDevice), "seq_len");
+    Q->h_seq_len[slot] = len;
     return LRM_OK;
 }
 

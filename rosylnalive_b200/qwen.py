@@ -35,7 +35,10 @@ N.extra_signatures({
     "lrm_qwen_reserve": [P, I32, I32],
     "lrm_qwen_prefill": [P, I32, PI32, PI32, PU32, PU32, PF32],
     "lrm_qwen_decode": [P, I32, PI32, PU32, PU32, PF32],
-    "lrm_qwen_decode_graph": [P, I32, PI32, PU32],
+    "lrm_qwen_decode_graph": [P, I32, PI32, PU32, U32],
+    "lrm_qwen_graph_kernels": [P, PI32],
+    "lrm_qwen_attention_ms": [P, PF32],
+    "lrm_qwen_truncate": [P, I32, I32],
     "lrm_qwen_decode_replay": [P, I32],
     "lrm_qwen_last_ids": [P, PU32],
     "lrm_qwen_sync": [P],
@@ -118,13 +121,27 @@ class QwenEngine:
                                             _p(logits, F32) if want_logits else None), "decode")
         return nxt, logits
 
-    def capture(self, slots, first_ids=None):
+    def capture(self, slots, first_ids=None, time_attention=False):
         """Captures the device-resident decode step for `slots` (inputs: the previous step's outputs)."""
         slots = np.ascontiguousarray(slots, np.int32)
         fid = None if first_ids is None else np.ascontiguousarray(first_ids, np.uint32)
         self._check(N.lib().lrm_qwen_decode_graph(self._h, len(slots), _p(slots, I32),
-                                                  _p(fid, U32) if fid is not None else None), "decode_graph")
+                                                  _p(fid, U32) if fid is not None else None,
+                                                  1 if time_attention else 0), "decode_graph")
         self._graph_batch = len(slots)
+
+    def graph_kernels(self) -> int:
+        v = ctypes.c_int32()
+        self._check(N.lib().lrm_qwen_graph_kernels(self._h, ctypes.byref(v)), "graph_kernels")
+        return v.value
+
+    def attention_ms(self) -> np.ndarray:
+        out = np.empty(self.cfg.layers, np.float32)
+        self._check(N.lib().lrm_qwen_attention_ms(self._h, _p(out, F32)), "attention_ms")
+        return out
+
+    def truncate(self, slot: int, length: int):
+        self._check(N.lib().lrm_qwen_truncate(self._h, slot, length), "truncate")
 
     def replay(self, steps: int):
         self._check(N.lib().lrm_qwen_decode_replay(self._h, steps), "decode_replay")

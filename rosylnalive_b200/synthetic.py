@@ -46,8 +46,36 @@ def random_tensor(name: str, shape, seed: int = 0) -> np.ndarray:
     return bf16_rne(x)
 
 
-def random_weights(cfg: QwenConfig, seed: int = 0) -> dict:
-    return {name: random_tensor(name, shape, seed) for name, shape in weight_shapes(cfg).items()}
+CHUNK_ROWS_ELEMS = 1 << 23  # tensors above this many elements are drawn in row chunks, one stream per chunk
+
+
+def _chunk(name, shape, seed, r0, r1):
+    g = np.random.default_rng([seed, zlib.crc32(name.encode()), r0])
+    x = g.standard_normal((r1 - r0,) + tuple(shape[1:]), dtype=np.float32) * np.float32(0.02)
+    return bf16_rne(x)
+
+
+def random_weights(cfg: QwenConfig, seed: int = 0, threads: int | None = None) -> dict:
+    """Every weight of `cfg`, each from its own stream (large matrices from one stream per block of rows), drawn on a
+    thread pool; the values do not depend on the thread count."""
+    import concurrent.futures as cf
+    import os
+
+    shapes = weight_shapes(cfg)
+    out = {}
+    with cf.ThreadPoolExecutor(max_workers=threads or min(32, os.cpu_count() or 1)) as ex:
+        futs = {}
+        for name, shape in shapes.items():
+            n = int(np.prod(shape))
+            if n <= CHUNK_ROWS_ELEMS or len(shape) != 2:
+                futs[name] = ex.submit(random_tensor, name, shape, seed)
+            else:
+                rows = max(1, CHUNK_ROWS_ELEMS // shape[1])
+                futs[name] = [ex.submit(_chunk, name, shape, seed, r0, min(shape[0], r0 + rows))
+                              for r0 in range(0, shape[0], rows)]
+        for name, f in futs.items():
+            out[name] = np.concatenate([c.result() for c in f]) if isinstance(f, list) else f.result()
+    return out
 
 
 def random_prompt(vocab: int, length: int, seed: int = 0, stream: str = "prompt") -> np.ndarray:
