@@ -191,6 +191,31 @@ typedef struct lrm_gemm_desc {
 } lrm_gemm_desc;
 lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *desc);
 
+/* Causal GQA attention of packed sequences (each starting at position 0), bf16 in/out, fp32 softmax and
+ * accumulation: q [T, q_heads, 128], k/v [T, kv_heads, 128] (K after QK-norm and RoPE), cu_seqlens int32 [nseq + 1]
+ * (device), out [T, q_heads, 128]. Replaces the reference's attention_gqa_causal
+ * (src/Lrm.Shaders/hlsl/kernels/attention/attention_gqa_causal.hlsl) for prefill on the bf16 path. */
+typedef struct lrm_prefill_attn_desc {
+    uint64_t q, k, v, out, cu_seqlens;
+    int32_t nseq, max_len, q_heads, kv_heads, head_dim;
+    float scale;
+} lrm_prefill_attn_desc;
+lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *desc);
+
+/* Decode attention, one query per row, over the paged bf16 KV cache: pool [pages][kv_heads][2][16][128] (K then V
+ * of a page and head, 8 KiB), page_table int32 [seqs][pages_per_seq], seq_len int32 [seqs] (keys per sequence,
+ * the new one included), slots int32 [batch] (device). q/out bf16 [batch][q_heads][128]; q_heads = 2 kv_heads.
+ * Each CTA streams pages_per_split pages of one (row, kv head); the splits' partial softmax states go to
+ * `workspace` (lrm_op_decode_attention_workspace bytes, 16-byte aligned) and a second kernel merges them. */
+typedef struct lrm_decode_attn_desc {
+    uint64_t q, pool, page_table, seq_len, slots, out, workspace;
+    int32_t batch, q_heads, kv_heads, head_dim, pages_per_seq, pages_per_split;
+    float scale;
+} lrm_decode_attn_desc;
+uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int32_t pages_per_seq,
+                                           int32_t pages_per_split);
+lrm_status lrm_op_decode_attention(void *stream, const lrm_decode_attn_desc *desc);
+
 /* ---- the Qwen3 forward engine (bf16 fast path) ---------------------------------------------------------------- */
 /*
  * The executor the reference plans but does not have (src/Lrm.Gpu.Exec/Placeholder.fs:1,

@@ -10,6 +10,7 @@
 #include "../../include/lrm_cuda.h"
 #include "gemm.h"
 #include "internal.h"
+#include "qwen.h"
 
 namespace lrm {
 
@@ -123,6 +124,73 @@ lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *d) {
     if (d->epilogue < 0 || d->epilogue > 4) return op_fail(LRM_ERR_ARGUMENT, "unknown epilogue");
     if (const char *why = gemm_check(a)) return op_fail(LRM_ERR_ARGUMENT, std::string("gemm: ") + why);
     return op_cuda(gemm_launch(a, device_sms(), (cudaStream_t)stream), "gemm");
+}
+
+lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d) {
+    if (!d) return op_fail(LRM_ERR_ARGUMENT, "descriptor is null");
+    if (d->head_dim != kHeadDim) return op_fail(LRM_ERR_ARGUMENT, "prefill attention needs head_dim 128");
+    if (d->nseq < 1 || d->nseq > 65535 || d->max_len < 1 || d->q_heads < 1 || d->q_heads > 65535 ||
+        d->kv_heads < 1 || d->q_heads % d->kv_heads)
+        return op_fail(LRM_ERR_ARGUMENT, "prefill attention: bad sizes (kv_heads must divide q_heads)");
+    if (!d->q || !d->k || !d->v || !d->out || !d->cu_seqlens || ((d->q | d->k | d->v | d->out) & 15))
+        return op_fail(LRM_ERR_ARGUMENT, "prefill attention: pointers must be non-null and 16-byte aligned");
+    if (!device_error_word()) return LRM_ERR_CUDA;
+    PrefillAttnArgs a;
+    a.q = (const __nv_bfloat16 *)d->q;
+    a.k = (const __nv_bfloat16 *)d->k;
+    a.v = (const __nv_bfloat16 *)d->v;
+    a.out = (__nv_bfloat16 *)d->out;
+    a.cu_seqlens = (const int32_t *)d->cu_seqlens;
+    a.nseq = d->nseq;
+    a.max_len = d->max_len;
+    a.q_heads = d->q_heads;
+    a.kv_heads = d->kv_heads;
+    a.scale_log2 = d->scale * 1.4426950408889634f;
+    return op_cuda(launch_prefill_attention(a, (cudaStream_t)stream), "prefill attention");
+}
+
+uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int32_t pages_per_seq,
+                                           int32_t pages_per_split) {
+    if (batch < 1 || kv_heads < 1 || pages_per_seq < 1 || pages_per_split < 1) return 0;
+    const uint64_t splits = (pages_per_seq + pages_per_split - 1) / pages_per_split;
+    const uint64_t states = (uint64_t)batch * kv_heads * splits * 2;
+    return states * (128 + 2) * sizeof(float);
+}
+
+// Fills the launch arguments shared by both decode-attention entry points; nullptr or the reason it refuses.
+static const char *decode_attn_args(const lrm_decode_attn_desc *d, DecodeAttnArgs &a) {
+    if (d->head_dim != kHeadDim) return "decode attention needs head_dim 128";
+    if (d->batch < 1 || d->batch > 65535 || d->kv_heads < 1 || d->kv_heads > 65535 || d->q_heads != 2 * d->kv_heads)
+        return "decode attention: bad sizes (q_heads must be 2 * kv_heads)";
+    if (d->pages_per_seq < 1 || d->pages_per_split < 1) return "decode attention: page counts must be positive";
+    if (!d->q || !d->pool || !d->page_table || !d->seq_len || !d->slots || !d->out)
+        return "decode attention: null pointer";
+    if ((d->q | d->pool | d->out) & 15) return "decode attention: q, pool and out must be 16-byte aligned";
+    a.q = (const __nv_bfloat16 *)d->q;
+    a.kv = KvLayout{(__nv_bfloat16 *)d->pool, (const int32_t *)d->page_table, d->pages_per_seq, d->kv_heads};
+    a.slots = (const int32_t *)d->slots;
+    a.seq_len = (const int32_t *)d->seq_len;
+    a.B = d->batch;
+    a.q_heads = d->q_heads;
+    a.pages_per_split = d->pages_per_split;
+    a.max_splits = (d->pages_per_seq + d->pages_per_split - 1) / d->pages_per_split;
+    a.scale_log2 = d->scale * 1.4426950408889634f;
+    a.out = (__nv_bfloat16 *)d->out;
+    return nullptr;
+}
+
+lrm_status lrm_op_decode_attention(void *stream, const lrm_decode_attn_desc *d) {
+    if (!d) return op_fail(LRM_ERR_ARGUMENT, "descriptor is null");
+    DecodeAttnArgs a;
+    if (const char *why = decode_attn_args(d, a)) return op_fail(LRM_ERR_ARGUMENT, why);
+    if (!d->workspace || (d->workspace & 15))
+        return op_fail(LRM_ERR_ARGUMENT, "decode attention: the workspace must be non-null and 16-byte aligned");
+    const size_t states = (size_t)a.B * d->kv_heads * a.max_splits * 2;
+    a.part_o = (float *)d->workspace;
+    a.part_ml = a.part_o + states * 128;
+    a.err = device_error_word();
+    if (!a.err) return LRM_ERR_CUDA;
+    return op_cuda(launch_decode_attention(a, (cudaStream_t)stream), "decode attention");
 }
 
 }  // extern "C"

@@ -19,11 +19,25 @@ class GemmDesc(ctypes.Structure):
                 ("splits", I32), ("out", U64), ("ldo", I32), ("resid", U64), ("ldr", I32), ("split_stride", U64)]
 
 
+class PrefillAttnDesc(ctypes.Structure):
+    _fields_ = [("q", U64), ("k", U64), ("v", U64), ("out", U64), ("cu_seqlens", U64), ("nseq", I32),
+                ("max_len", I32), ("q_heads", I32), ("kv_heads", I32), ("head_dim", I32), ("scale", ctypes.c_float)]
+
+
+class DecodeAttnDesc(ctypes.Structure):
+    _fields_ = [("q", U64), ("pool", U64), ("page_table", U64), ("seq_len", U64), ("slots", U64), ("out", U64),
+                ("workspace", U64), ("batch", I32), ("q_heads", I32), ("kv_heads", I32), ("head_dim", I32),
+                ("pages_per_seq", I32), ("pages_per_split", I32), ("scale", ctypes.c_float)]
+
+
 N.extra_signatures({
     "lrm_op_set_device": [I32],
     "lrm_op_error_word": [ctypes.POINTER(U32), I32],
     "lrm_op_gemm_bf16": [P, ctypes.POINTER(GemmDesc)],
-})
+    "lrm_op_prefill_attention": [P, ctypes.POINTER(PrefillAttnDesc)],
+    "lrm_op_decode_attention_workspace": [I32, I32, I32, I32],
+    "lrm_op_decode_attention": [P, ctypes.POINTER(DecodeAttnDesc)],
+}, {"lrm_op_decode_attention_workspace": U64})
 
 
 def _stream(stream):
@@ -53,3 +67,23 @@ def gemm(a, b, out, epilogue=GEMM_F32, resid=None, splits=1, bn=0, ldo=None, spl
                  resid.data_ptr() if resid is not None else 0, resid.shape[-1] if resid is not None else 0,
                  split_stride)
     N.check(N.lib().lrm_op_gemm_bf16(_stream(stream), ctypes.byref(d)), None, "gemm")
+
+
+def prefill_attention(q, k, v, out, cu_seqlens, max_len, scale, stream=None):
+    """Causal GQA attention of packed sequences: q [T, qh, 128], k/v [T, kvh, 128], cu_seqlens int32 [nseq + 1]."""
+    d = PrefillAttnDesc(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), cu_seqlens.data_ptr(),
+                        cu_seqlens.numel() - 1, max_len, q.shape[1], k.shape[1], q.shape[2], scale)
+    N.check(N.lib().lrm_op_prefill_attention(_stream(stream), ctypes.byref(d)), None, "prefill_attention")
+
+
+def decode_attention_workspace(batch, kv_heads, pages_per_seq, pages_per_split) -> int:
+    return int(N.lib().lrm_op_decode_attention_workspace(batch, kv_heads, pages_per_seq, pages_per_split))
+
+
+def decode_attention(q, pool, page_table, seq_len, slots, out, workspace, pages_per_split, scale, stream=None):
+    """Paged decode attention: q [B, qh, 128], pool [pages, kvh, 2, 16, 128], page_table int32 [seqs, pages_per_seq],
+    seq_len int32 [seqs], slots int32 [B]."""
+    d = DecodeAttnDesc(q.data_ptr(), pool.data_ptr(), page_table.data_ptr(), seq_len.data_ptr(), slots.data_ptr(),
+                       out.data_ptr(), workspace.data_ptr(), q.shape[0], q.shape[1], pool.shape[1], q.shape[2],
+                       page_table.shape[1], pages_per_split, scale)
+    N.check(N.lib().lrm_op_decode_attention(_stream(stream), ctypes.byref(d)), None, "decode_attention")
