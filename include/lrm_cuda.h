@@ -216,6 +216,18 @@ uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int3
                                            int32_t pages_per_split);
 lrm_status lrm_op_decode_attention(void *stream, const lrm_decode_attn_desc *desc);
 
+/* Decode attention that allocates nothing. No counterpart in the reference: it is for callers that cannot allocate
+ * device memory (a host that sizes all device memory once up front, as the reference's device contract does with
+ * its one CreateHeap; a serving loop with a fixed memory budget; code inside a stream capture or a host callback),
+ * and so cannot provide lrm_op_decode_attention's workspace. It runs the same kernels with their split-K scratch in
+ * a 16 MiB array built into the library (every GPU that loads the library holds it until the process exits).
+ * desc->workspace must be 0. A call needing more than LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES of scratch
+ * (lrm_op_decode_attention_workspace) is refused with LRM_ERR_ARGUMENT. The first call on a device looks up the
+ * array's device address with that device current; make it before any stream capture. Nothing in the scratch must
+ * start at zero. All calls on a device share the array, so calls that overlap on the GPU race on it. */
+#define LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES (16u << 20)
+lrm_status lrm_op_decode_attention_static(void *stream, const lrm_decode_attn_desc *desc);
+
 /* ---- the Qwen3 forward engine (bf16 fast path) ---------------------------------------------------------------- */
 /*
  * The executor the reference plans but does not have (src/Lrm.Gpu.Exec/Placeholder.fs:1,

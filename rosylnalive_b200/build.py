@@ -30,6 +30,7 @@ SOURCES = [
     "qwen_kernels.cu",
     "flash_prefill.cu",
     "qwen_engine.cu",
+    "decode_attn_static.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

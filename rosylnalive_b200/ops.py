@@ -37,7 +37,11 @@ N.extra_signatures({
     "lrm_op_prefill_attention": [P, ctypes.POINTER(PrefillAttnDesc)],
     "lrm_op_decode_attention_workspace": [I32, I32, I32, I32],
     "lrm_op_decode_attention": [P, ctypes.POINTER(DecodeAttnDesc)],
+    "lrm_op_decode_attention_static": [P, ctypes.POINTER(DecodeAttnDesc)],
 }, {"lrm_op_decode_attention_workspace": U64})
+
+# Scratch built into liblrmcuda.so for lrm_op_decode_attention_static (LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES).
+DECODE_ATTN_STATIC_SCRATCH_BYTES = 16 << 20
 
 
 def _stream(stream):
@@ -87,3 +91,14 @@ def decode_attention(q, pool, page_table, seq_len, slots, out, workspace, pages_
                        out.data_ptr(), workspace.data_ptr(), q.shape[0], q.shape[1], pool.shape[1], q.shape[2],
                        page_table.shape[1], pages_per_split, scale)
     N.check(N.lib().lrm_op_decode_attention(_stream(stream), ctypes.byref(d)), None, "decode_attention")
+
+
+def decode_attention_static(q, pool, page_table, seq_len, slots, out, pages_per_split, scale, stream=None):
+    """decode_attention for callers that cannot allocate device memory: the split scratch is the 16 MiB array built
+    into liblrmcuda.so (DECODE_ATTN_STATIC_SCRATCH_BYTES); the caller passes only inputs and the output. Calls that
+    overlap on the GPU share that array and race; the first call on a device should come before any stream capture."""
+    d = DecodeAttnDesc(q.data_ptr(), pool.data_ptr(), page_table.data_ptr(), seq_len.data_ptr(), slots.data_ptr(),
+                       out.data_ptr(), 0, q.shape[0], q.shape[1], pool.shape[1], q.shape[2], page_table.shape[1],
+                       pages_per_split, scale)
+    N.check(N.lib().lrm_op_decode_attention_static(_stream(stream), ctypes.byref(d)), None,
+            "decode_attention_static")
