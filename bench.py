@@ -47,6 +47,10 @@ def parse():
     p.add_argument("--no-prefill-bench", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample, seconds")
+    p.add_argument("--layers", type=int, default=28, help="decoder layers (profiling cases use fewer)")
+    p.add_argument("--no-decode", action="store_true", help="only the config-4 prefill part")
+    p.add_argument("--prefill-batch", type=int, default=16, help="config-4 prompts per job")
+    p.add_argument("--prefill-len", type=int, default=2048, help="config-4 prompt length")
     return p.parse_args()
 
 
@@ -199,28 +203,21 @@ def run_ours(args, dist):
 
     pk, pk_kind = peaks()
     cfg = S.QWEN3_0_6B
+    if args.layers != cfg.layers:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, layers=args.layers)
     B, ctx, K, W = args.batch, args.context, args.steps, args.warmup
     weights = S.random_weights(cfg, seed=0)
-    max_pos = (ctx + W + K + 16 + 15) // 16 * 16
+    max_pos = (max(ctx + W + K + 16, args.prefill_len) + 15) // 16 * 16
     cos, sin = R.t_spec(R.QWEN3_INV_FREQ_BITS, max_pos)
     chunk = max(1, min(B, 32768 // ctx))
-    eng = Qw.QwenEngine(cfg, weights, cos, sin, device=dist.local, max_seqs=max(B, 16), max_tokens=32768,
+    pf_seqs = max(1, args.prefill_batch // dist.world)
+    max_tokens = max(32768 if not args.no_decode else 0, pf_seqs * args.prefill_len)
+    eng = Qw.QwenEngine(cfg, weights, cos, sin, device=dist.local, max_seqs=max(B, pf_seqs), max_tokens=max_tokens,
                         max_batch=B, max_pos=max_pos)
     stream = torch.cuda.ExternalStream(eng.stream)
     slots = np.arange(B, dtype=np.int32)
-
-    # KV prefill from random ids (setup, not timed).
-    prompts = S.random_prompts(cfg.vocab, B, ctx, seed=1000 + dist.rank)
-    first = []
-    for i in range(0, B, chunk):
-        nxt, _ = eng.prefill(slots[i:i + chunk], list(prompts[i:i + chunk]))
-        first.extend(nxt.tolist())
-    eng.capture(slots, np.array(first, np.uint32))
-    launches_per_step = eng.graph_kernels()
-    eng.replay(W)
-    eng.sync()
-    start_len = ctx + W
-    ids_at_start = eng.last_ids()
 
     def timed(fn):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -234,6 +231,31 @@ def run_ours(args, dist):
         torch.cuda.synchronize()
         dist.barrier()
         return dist.max(e0.elapsed_time(e1))
+
+    if args.no_decode:
+        prefill = prefill_bench(eng, cfg, dist, pk, stream, timed, args.prefill_batch, args.prefill_len)
+        eng.close()
+        if dist.rank == 0:
+            print(json.dumps({"metric": METRIC, "value": prefill["value"], "unit": "tok/s", "n_gpus": dist.world,
+                              "steps": 3, "warmup": 2, "ms_per_step": prefill["ms_per_prefill"],
+                              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                              "data": "synthetic", "config": {"workload": prefill["workload"],
+                                                              "layers": cfg.layers},
+                              "prefill": prefill}), flush=True)
+        return
+
+    # KV prefill from random ids (setup, not timed).
+    prompts = S.random_prompts(cfg.vocab, B, ctx, seed=1000 + dist.rank)
+    first = []
+    for i in range(0, B, chunk):
+        nxt, _ = eng.prefill(slots[i:i + chunk], list(prompts[i:i + chunk]))
+        first.extend(nxt.tolist())
+    eng.capture(slots, np.array(first, np.uint32))
+    launches_per_step = eng.graph_kernels()
+    eng.replay(W)
+    eng.sync()
+    start_len = ctx + W
+    ids_at_start = eng.last_ids()
 
     gpu_ids = [torch.cuda.get_device_properties(i).uuid for i in range(torch.cuda.device_count())]
     sampler = ClockSampler([f"GPU-{u}" if not str(u).startswith("GPU-") else str(u) for u in gpu_ids]
@@ -290,7 +312,7 @@ def run_ours(args, dist):
 
     prefill = None
     if not args.no_prefill_bench:
-        prefill = prefill_bench(eng, cfg, dist, pk, stream, timed)
+        prefill = prefill_bench(eng, cfg, dist, pk, stream, timed, args.prefill_batch, args.prefill_len)
     eng.close()
 
     cpu = None
@@ -304,8 +326,9 @@ def run_ours(args, dist):
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": K, "warmup": W,
                 "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "config5: Qwen3-0.6B bf16 greedy decode, 64 seqs/GPU, 4096-token paged KV "
-                                       "(16-token pages), random-init weights N(0,0.02), random prompt ids",
+                "config": {"workload": f"config5: Qwen3-0.6B bf16 greedy decode, {B} seqs/GPU, {ctx}-token paged KV "
+                                       "(16-token pages), random-init weights N(0,0.02), random prompt ids"
+                                       + ("" if cfg.layers == 28 else f" [profiling case: {cfg.layers} layers]"),
                            "model": "Qwen3-0.6B architecture", "global_batch": B * dist.world, "seq_len": ctx,
                            "parallelism": f"dp{dist.world} (independent sequences per GPU, no collective)",
                            "l2": "inputs larger than L2 (32 GB KV cache), no flush"},
@@ -332,12 +355,11 @@ def profile_traffic(kernel: str, algorithmic_bytes: float):
     return float(d["dram_bytes_per_algorithmic_byte"]) * algorithmic_bytes
 
 
-def prefill_bench(eng, cfg, dist, pk, stream, timed):
+def prefill_bench(eng, cfg, dist, pk, stream, timed, batch=16, L=2048):
     """16 x 2048-token prompts per job, 16 / N per GPU (strong scaling)."""
     from rosylnalive_b200 import synthetic as S
 
-    nseq = max(1, 16 // dist.world)
-    L = 2048
+    nseq = max(1, batch // dist.world)
     prompts = list(S.random_prompts(cfg.vocab, nseq, L, seed=2000 + dist.rank))
     slots = np.arange(nseq, dtype=np.int32)
     for _ in range(2):
