@@ -30,6 +30,10 @@ static thread_local std::string g_thread_error;
 void set_thread_error(const std::string &m) { g_thread_error = m; }
 std::string thread_error() { return g_thread_error; }
 
+static thread_local bool g_pdl = false;
+bool pdl_enabled() { return g_pdl; }
+void set_pdl(bool on) { g_pdl = on; }
+
 static std::string fmt(const char *f, ...) {
     char buf[1024];
     va_list ap;

@@ -10,6 +10,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "internal.h"
 #include "qwen.h"
 
 namespace lrm {
@@ -73,6 +74,8 @@ __global__ void __launch_bounds__(NWARP * 32) flash_prefill_kernel(PrefillAttnAr
     const uint32_t sK = sQ + BQ * 256;          // 2 buffers
     const uint32_t sV = sK + 2 * BKV * 256;     // 2 buffers
 
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int seq = blockIdx.z, h = blockIdx.y;
     const int start = a.cu_seqlens[seq];
     const int len = a.cu_seqlens[seq + 1] - start;
@@ -225,8 +228,7 @@ cudaError_t launch_prefill_attention(const PrefillAttnArgs &a, cudaStream_t st) 
         configured[dev & 63] = true;
     }
     dim3 grid((a.max_len + BQ - 1) / BQ, a.q_heads, a.nseq);
-    flash_prefill_kernel<<<grid, NWARP * 32, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_kernel(flash_prefill_kernel, grid, dim3(NWARP * 32), smem, st, a);
 }
 
 }  // namespace lrm

@@ -26,6 +26,9 @@ struct GemmArgs {
     float *partial;
     size_t split_stride;  // elements between split slices of `partial`
     uint32_t *err;        // device error word: bounded waits write a code here
+    // Which operand no earlier kernel writes (1 = A, 2 = B, 0 = neither): under programmatic dependent launch its
+    // first k-blocks are prefetched before the kernel waits for the previous one (decode: the weights).
+    int independent;
 };
 
 // nullptr when the arguments are valid, else the reason.

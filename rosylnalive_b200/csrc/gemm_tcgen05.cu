@@ -27,6 +27,7 @@
 #include <string.h>
 
 #include "gemm.h"
+#include "internal.h"
 #include "ptx.cuh"
 
 namespace lrm {
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    ptx::griddep_launch();
 
     // Tile t -> (split, m block, n block); n is fastest so consecutive CTAs share the A rows.
     auto decode_tile = [&](int t, int &split, int &mb, int &nb) {
@@ -117,6 +119,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ptx::elect_one()) {
             uint32_t it = 0;
             bool ok = true;
+            // Under programmatic dependent launch, the operand no earlier kernel writes (the weights) is fetched for
+            // the first stages of the first tile before waiting for the previous kernel; the other operand after.
+            int pre = 0;
+            if (args.independent && (int)blockIdx.x < total) {
+                int split, mb, nb, k0, k1;
+                decode_tile(blockIdx.x, split, mb, nb);
+                kb_range(split, k0, k1);
+                pre = min(C::STAGES, max(0, k1 - k0));
+                for (int j = 0; j < pre; ++j) {
+                    uint8_t *sa = smem + j * C::STAGE_BYTES;
+                    ptx::mbar_arrive_expect_tx(&full[j], C::STAGE_BYTES);
+                    if (args.independent == 1)
+                        ptx::tma_load_2d(sa, &tmap_a, &full[j], (k0 + j) * BK, mb * BM);
+                    else
+                        ptx::tma_load_2d(sa + C::A_BYTES, &tmap_b, &full[j], (k0 + j) * BK, nb * BN);
+                }
+            }
+            ptx::griddep_wait();
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 int split, mb, nb, k0, k1;
                 decode_tile(t, split, mb, nb);
@@ -124,12 +144,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kb = k0; kb < k1; ++kb, ++it) {
                     int s = it % C::STAGES;
                     uint32_t ph = (it / C::STAGES) & 1;
+                    uint8_t *sa = smem + s * C::STAGE_BYTES;
+                    uint8_t *sb = sa + C::A_BYTES;
+                    if ((int)it < pre) {  // armed above; only the dependent operand is left
+                        if (args.independent == 1)
+                            ptx::tma_load_2d(sb, &tmap_b, &full[s], kb * BK, nb * BN);
+                        else
+                            ptx::tma_load_2d(sa, &tmap_a, &full[s], kb * BK, mb * BM);
+                        continue;
+                    }
                     if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, 0x1001)) {
                         ok = false;
                         break;
                     }
-                    uint8_t *sa = smem + s * C::STAGE_BYTES;
-                    uint8_t *sb = sa + C::A_BYTES;
                     ptx::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
                     ptx::tma_load_2d(sa, &tmap_a, &full[s], kb * BK, mb * BM);
                     ptx::tma_load_2d(sb, &tmap_b, &full[s], kb * BK, nb * BN);
@@ -141,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, err, 0x1002);
         }
     } else if (warp == 1) {
+        ptx::griddep_wait();
         if (ptx::elect_one()) {
             constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
             uint32_t it = 0, local = 0;
@@ -176,7 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::mbar_wait(mma_done, 0, err, 0x1005);
         }
     } else {
-        // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds rows 32q..32q+31 of the tile.
+        // Epilogue warps 2..5: TMEM lane quarter q = warp % 4 holds rows 32q..32q+31 of the tile. They read the
+        // residual and write outputs that the previous kernel may still use, so they wait for it first.
+        ptx::griddep_wait();
         const int q = warp & 3;
         uint32_t local = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
@@ -343,8 +373,7 @@ cudaError_t launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const GemmAr
     int m_tiles = (args.M + BM - 1) / BM, n_tiles = (args.N + BN - 1) / BN;
     int total = m_tiles * n_tiles * args.splits;
     int grid = total < sms ? total : sms;
-    gemm_kernel<BN, EPI><<<grid, kThreads, C::SMEM_BYTES, stream>>>(ta, tb, args);
-    return cudaGetLastError();
+    return launch_kernel(gemm_kernel<BN, EPI>, dim3(grid), dim3(kThreads), C::SMEM_BYTES, stream, ta, tb, args);
 }
 
 template <int BN>

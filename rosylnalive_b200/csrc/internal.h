@@ -27,6 +27,29 @@ bool catalog_kernel_present(uint32_t kernel);
 void set_thread_error(const std::string &msg);
 std::string thread_error();
 
+// Whether launches on this thread use programmatic dependent launch (the engine turns it on around its own
+// sequences; every kernel that can be launched this way calls griddepcontrol.wait before it touches data that the
+// previous kernel writes).
+bool pdl_enabled();
+void set_pdl(bool on);
+
+// Launches `kernel` with programmatic stream serialization when pdl_enabled().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, ((KArgs)args)...);
+}
+
 }  // namespace lrm
 
 #define LRM_CATALOG_KERNELS 14

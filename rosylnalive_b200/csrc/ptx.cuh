@@ -156,6 +156,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may start before the
+// previous kernel in the stream has finished: griddep_wait blocks until that kernel has completed and its memory is
+// visible (a no-op when the launch had no such dependency); griddep_launch lets the next kernel's CTAs be scheduled
+// once every CTA of this kernel has started or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Named barrier among `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -66,6 +66,7 @@ struct lrm_qwen_s {
     std::string error;
     // weights
     uint8_t *wmem = nullptr;
+    size_t wbytes = 0;
     __nv_bfloat16 *embed = nullptr, *final_norm = nullptr;
     std::vector<Layer> layers;
     float *cos_t = nullptr, *sin_t = nullptr;
@@ -149,6 +150,11 @@ static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, i
     a.ldr = ldr;
     a.split_stride = split_stride;
     a.err = Q->err;
+    // The weight operand is written by no kernel, so under programmatic dependent launch it is prefetched early.
+    auto is_weight = [&](const void *p) {
+        return (const uint8_t *)p >= Q->wmem && (const uint8_t *)p < Q->wmem + Q->wbytes;
+    };
+    a.independent = is_weight(A) ? 1 : (is_weight(B) ? 2 : 0);
     if (const char *why = gemm_check(a)) return qfail(Q, LRM_ERR_ARGUMENT, std::string("gemm: ") + why);
     return qcuda(Q, gemm_launch(a, Q->sms, Q->stream), "gemm");
 }
@@ -161,7 +167,14 @@ static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, i
 #define KTRY(Q, call, what) QTRY(Q, call, what)
 
 // One decode step over device-resident ids/slots (Q->ids[0..B), Q->d_slots) -> Q->next; logits in Q->partial.
+// Turns programmatic dependent launch on for the kernels an engine sequence launches on this thread.
+struct PdlScope {
+    PdlScope() { set_pdl(true); }
+    ~PdlScope() { set_pdl(false); }
+};
+
 static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
+    PdlScope pdl;
     const lrm_qwen_config &c = Q->c;
     cudaStream_t st = Q->stream;
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
@@ -289,6 +302,7 @@ lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *cfg, lrm_qwen 
                        2 * H + 2 * kHeadDim;
     size_t wbytes = ((size_t)V * H + H) * 2 + (size_t)c.layers * (per_layer * 2 + 8 * 256) + 4096;
     QTRY(Q.get(), cudaMalloc(&Q->wmem, wbytes), "weights");
+    Q->wbytes = wbytes;
     QTRY(Q.get(), cudaMemset(Q->wmem, 0, wbytes), "weights");
     uint8_t *p = Q->wmem;
     Q->embed = carve<__nv_bfloat16>(p, (size_t)V * H);
@@ -498,6 +512,7 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
     for (int i = 0; i < nseq; ++i)
         QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slots[i], &lens[i], 4, cudaMemcpyHostToDevice, st), "seq_len");
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
+    PdlScope pdl;
     KTRY(Q, launch_embed_norm(Q->ids, T, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
          "embed_norm");
     for (int l = 0; l < c.layers; ++l) {

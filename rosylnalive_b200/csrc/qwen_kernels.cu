@@ -12,6 +12,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "internal.h"
 #include "ptx.cuh"
 #include "qwen.h"
 
@@ -40,11 +41,18 @@ __device__ __forceinline__ float block_sum256(float v, float *red) {
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
 
+__device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    return make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+}
+
 // ---- embed + norm -------------------------------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t *ids, const __nv_bfloat16 *embed, int hidden,
                                                          int vocab, const __nv_bfloat16 *w, float eps, float *x,
                                                          __nv_bfloat16 *xn) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     __shared__ float red[8];
     const int t = blockIdx.x;
     uint32_t id = ids[t];
@@ -63,33 +71,61 @@ __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t *ids, co
 
 // ---- residual + split reduce + norm --------------------------------------------------------------------------------
 
+// One block per row, 4 consecutive columns per thread (hidden % 4 == 0). The split partials are added in split
+// order, but their loads are issued 8 at a time so a 16-way split costs about two memory latencies, not sixteen.
 __global__ void __launch_bounds__(256) resid_norm_kernel(float *x, const float *partial, int splits,
                                                          size_t split_stride, int hidden, const __nv_bfloat16 *w,
                                                          float eps, __nv_bfloat16 *xn) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     __shared__ float red[8];
     const int t = blockIdx.x;
-    float *xr = x + (size_t)t * hidden;
+    float4 *xr = reinterpret_cast<float4 *>(x + (size_t)t * hidden);
+    const float4 *pr = reinterpret_cast<const float4 *>(partial + (size_t)t * hidden);
+    const size_t stride4 = split_stride / 4;
+    const int n4 = hidden / 4;
     float ss = 0.f;
-    for (int c = threadIdx.x; c < hidden; c += 256) {
-        float v = xr[c];
-        for (int s = 0; s < splits; ++s) v += partial[s * split_stride + (size_t)t * hidden + c];
+    for (int c = threadIdx.x; c < n4; c += 256) {
+        float4 v = xr[c];
+        int s = 0;
+        for (; s + 8 <= splits; s += 8) {
+            float4 q[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) q[j] = pr[(s + j) * stride4 + c];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                v.x += q[j].x;
+                v.y += q[j].y;
+                v.z += q[j].z;
+                v.w += q[j].w;
+            }
+        }
+        for (; s < splits; ++s) {
+            const float4 q = pr[s * stride4 + c];
+            v.x += q.x;
+            v.y += q.y;
+            v.z += q.z;
+            v.w += q.w;
+        }
         if (splits) xr[c] = v;
-        ss += v * v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
-    float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
-    for (int c = threadIdx.x; c < hidden; c += 256)
-        xn[(size_t)t * hidden + c] = __float2bfloat16_rn(xr[c] * r * bf(w[c]));
+    const float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
+    for (int c = threadIdx.x; c < n4; c += 256) {
+        const float4 v = xr[c];
+        const uint2 wv = *reinterpret_cast<const uint2 *>(w + 4 * c);
+        *reinterpret_cast<uint2 *>(xn + (size_t)t * hidden + 4 * c) =
+            pack4(v.x * r * __uint_as_float(wv.x << 16), v.y * r * __uint_as_float(wv.x & 0xFFFF0000u),
+                  v.z * r * __uint_as_float(wv.y << 16), v.w * r * __uint_as_float(wv.y & 0xFFFF0000u));
+    }
 }
 
 // ---- q/k norm + RoPE + KV append --------------------------------------------------------------------------------
 
-__device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
-    __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
-    return make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
-}
-
 // One warp per (token, head row); lane l owns dims 4l..4l+3. Head rows 0..q-1 are q, then kv k rows, then kv v rows.
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(QkvArgs a) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     const int warp_global = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int rows = a.q_heads + 2 * a.kv_heads;
@@ -145,6 +181,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(QkvArgs a) {
 
 __global__ void swiglu_reduce_kernel(const float *partial, int splits, size_t split_stride, int T, int inter,
                                      __nv_bfloat16 *act) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= (size_t)T * inter) return;
     int t = (int)(e / inter), j = (int)(e % inter);
@@ -160,6 +198,8 @@ __global__ void swiglu_reduce_kernel(const float *partial, int splits, size_t sp
 // ---- argmax -------------------------------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V, uint32_t *out) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ int nan_any;
@@ -211,12 +251,16 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V
 }
 
 __global__ void gather_rows_kernel(const __nv_bfloat16 *src, const int32_t *idx, int cols, __nv_bfloat16 *dst) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     const int r = blockIdx.x;
     const __nv_bfloat16 *s = src + (size_t)idx[r] * cols;
     for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[(size_t)r * cols + c] = s[c];
 }
 
 __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     int slot = slots[b];
@@ -249,6 +293,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
     uint64_t *full = (uint64_t *)(red_l + 8);
     uint64_t *empty = full + ST;
 
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots[b];
     const int len = a.seq_len[slot];
@@ -416,6 +462,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
 }
 
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     const int b = blockIdx.x, qh = blockIdx.y, d = threadIdx.x;
     const int h = qh / 2, hh = qh % 2;
     const int len = a.seq_len[a.slots[b]];
@@ -438,43 +486,38 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
 
 cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
                               const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st) {
-    embed_norm_kernel<<<T, 256, 0, st>>>(ids, embed, hidden, vocab, w, eps, x, xn);
-    return cudaGetLastError();
+    return launch_kernel(embed_norm_kernel, dim3(T), dim3(256), 0, st, ids, embed, hidden, vocab, w, eps, x, xn);
 }
 
 cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
                               const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st) {
-    resid_norm_kernel<<<T, 256, 0, st>>>(x, partial, splits, split_stride, hidden, w, eps, xn);
-    return cudaGetLastError();
+    return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, partial, splits, split_stride, hidden, w,
+                         eps, xn);
 }
 
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs &a, cudaStream_t st) {
     const int warps = a.T * (a.q_heads + 2 * a.kv_heads);
-    qk_norm_rope_kv_kernel<<<(warps + 7) / 8, 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_kernel(qk_norm_rope_kv_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, a);
 }
 
 cudaError_t launch_swiglu_reduce(const float *partial, int splits, size_t split_stride, int T, int inter,
                                  __nv_bfloat16 *act, cudaStream_t st) {
     size_t n = (size_t)T * inter;
-    swiglu_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partial, splits, split_stride, T, inter, act);
-    return cudaGetLastError();
+    return launch_kernel(swiglu_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, partial, splits,
+                         split_stride, T, inter, act);
 }
 
 cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st) {
-    argmax_kernel<<<R, 1024, 0, st>>>(logits, V, out);
-    return cudaGetLastError();
+    return launch_kernel(argmax_kernel, dim3(R), dim3(1024), 0, st, logits, V, out);
 }
 
 cudaError_t launch_gather_rows(const __nv_bfloat16 *src, const int32_t *idx, int R, int cols, __nv_bfloat16 *dst,
                                cudaStream_t st) {
-    gather_rows_kernel<<<R, 256, 0, st>>>(src, idx, cols, dst);
-    return cudaGetLastError();
+    return launch_kernel(gather_rows_kernel, dim3(R), dim3(256), 0, st, src, idx, cols, dst);
 }
 
 cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos, cudaStream_t st) {
-    advance_kernel<<<(B + 127) / 128, 128, 0, st>>>(slots, B, seq_len, tok_pos);
-    return cudaGetLastError();
+    return launch_kernel(advance_kernel, dim3((B + 127) / 128), dim3(128), 0, st, slots, B, seq_len, tok_pos);
 }
 
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
@@ -489,12 +532,10 @@ cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         configured[dev & 63] = true;
     }
-    dim3 grid(a.max_splits, a.kv.kv_heads, a.B);
-    decode_attn_kernel<ST><<<grid, 160, smem, st>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_kernel(decode_attn_kernel<ST>, dim3(a.max_splits, a.kv.kv_heads, a.B), dim3(160), smem, st,
+                                  a);
     if (e != cudaSuccess) return e;
-    decode_combine_kernel<<<dim3(a.B, a.q_heads), 128, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_kernel(decode_combine_kernel, dim3(a.B, a.q_heads), dim3(128), 0, st, a);
 }
 
 }  // namespace lrm
