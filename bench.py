@@ -64,10 +64,16 @@ def peaks():
 
 
 class Dist:
-    def __init__(self):
+    """One process per GPU (torchrun's RANK / LOCAL_RANK / WORLD_SIZE). Sequences are independent, so the process
+    group carries only the timing barrier and the max-over-ranks reduction; `backend` is nccl on GPUs (gloo in the
+    CPU tests of this plumbing). A rank that stops answering ends the others' next collective after `timeout_s`."""
+
+    def __init__(self, backend: str = "nccl", timeout_s: float = 600.0):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend
+        self.timeout_s = timeout_s
         self.pg = None
 
     def init(self):
@@ -75,12 +81,13 @@ class Dist:
 
         import torch
 
-        torch.cuda.set_device(self.local)
+        if self.backend == "nccl":
+            torch.cuda.set_device(self.local)
         if self.world > 1:
             import torch.distributed as dist
 
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device(f"cuda:{self.local}"))
+            kw = {"device_id": torch.device(f"cuda:{self.local}")} if self.backend == "nccl" else {}
+            dist.init_process_group(self.backend, timeout=datetime.timedelta(seconds=self.timeout_s), **kw)
             self.pg = dist
 
     def barrier(self):
@@ -92,7 +99,8 @@ class Dist:
             return v
         import torch
 
-        t = torch.tensor([v], device=f"cuda:{self.local}", dtype=torch.float64)
+        dev = f"cuda:{self.local}" if self.backend == "nccl" else "cpu"
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
