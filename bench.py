@@ -341,7 +341,7 @@ def run_ours(args, dist):
                            "parallelism": f"dp{dist.world} (independent sequences per GPU, no collective)",
                            "l2": "inputs larger than L2 (32 GB KV cache), no flush"},
                 "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
-                "gpu_launches": launches_per_step * K, "roofline": roofline, "step_roofline": step_roof,
+                "gpu_launches": launches_per_step * K * dist.world, "roofline": roofline, "step_roofline": step_roof,
                 "prefill": prefill, "cpu_baseline": cpu, "clocks": clocks}
         print(json.dumps(line), flush=True)
 

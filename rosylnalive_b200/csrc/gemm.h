@@ -8,7 +8,22 @@
 
 namespace lrm {
 
-enum GemmEpi : int { EPI_F32 = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_BF16 = 4 };
+enum GemmEpi : int { EPI_F32 = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_BF16 = 4, EPI_QKV = 5 };
+
+// The q/k/v epilogue (EPI_QKV): the output columns are head rows of 128 (q heads, then k heads, then v heads); each
+// thread owns one token row of one head, applies the per-head RMSNorm (q_norm / k_norm) and NeoX RoPE to q and k at
+// the token's position, and writes bf16 q to q_out [T][q_heads][128], k and v to k_out / v_out [T][kv_heads][128]
+// and into the paged cache (pool [pages][kv_heads][2][16][128], page table [slots][pages_per_seq]).
+struct QkvEpilogue {
+    __nv_bfloat16 *q_out, *k_out, *v_out, *pool;
+    const int32_t *pages;
+    int pages_per_seq;
+    int q_heads, kv_heads;
+    const __nv_bfloat16 *q_norm, *k_norm;
+    float eps;
+    const float *cos_t, *sin_t;  // [max_pos][64]
+    const int32_t *tok_slot, *tok_pos;
+};
 
 struct GemmArgs {
     int M, N, K;
@@ -29,6 +44,7 @@ struct GemmArgs {
     // Which operand no earlier kernel writes (1 = A, 2 = B, 0 = neither): under programmatic dependent launch its
     // first k-blocks are prefetched before the kernel waits for the previous one (decode: the weights).
     int independent;
+    QkvEpilogue qkv;  // EPI_QKV only
 };
 
 // nullptr when the arguments are valid, else the reason.

@@ -20,6 +20,8 @@
 //   EPI_PARTIAL  swap-AB split-K partials, transposed: partial[split][n][m] = acc (M indexes weight rows and N
 //                tokens, so this writes Y[token][feature] partial sums for a consumer to reduce in a fixed order)
 //   EPI_BF16     out_bf16[m, n] = bf16(acc)
+//   EPI_QKV      prefill q/k/v: per 128-column head, QK-RMSNorm and RoPE for q and k, then bf16 q/k/v written to their
+//                contiguous buffers and k/v appended to the paged KV cache (QkvEpilogue)
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -220,7 +222,114 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
             const int n0 = nb * BN;
             const bool has_k = k1 > k0;
-            if (EPI == EPI_SWIGLU) {
+            if (EPI == EPI_QKV) {
+                // Two light passes over TMEM per 128-column head: the sum of squares, then the RoPE pairs (i, i + 64)
+                // sixteen at a time, normalised, rotated, rounded to bf16 and stored; few registers, vector loads.
+                const QkvEpilogue &E = args.qkv;
+                const bool row_ok = row < args.M;
+                const int pos = row_ok ? E.tok_pos[row] : 0;
+                const int slot = row_ok ? E.tok_slot[row] : 0;
+#pragma unroll 1
+                for (int hh = 0; hh < BN / 128; ++hh) {
+                    const uint32_t t_head = t_row + hh * 128;
+                    const int head_row = (n0 + hh * 128) / 128;
+                    const bool is_q = head_row < E.q_heads, is_k = !is_q && head_row < E.q_heads + E.kv_heads;
+                    const bool rotate = is_q || is_k;
+                    float r = 1.f;
+                    if (rotate) {
+                        float ss = 0.f;
+#pragma unroll 1
+                        for (int c = 0; c < 8; c += 2) {
+                            uint32_t u0[16], u1[16];
+                            ptx::tmem_ld16(t_head + c * 16, u0);
+                            ptx::tmem_ld16(t_head + c * 16 + 16, u1);
+                            ptx::tmem_ld_wait();
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const float a = __uint_as_float(u0[j]), b = __uint_as_float(u1[j]);
+                                ss = fmaf(a, a, ss);
+                                ss = fmaf(b, b, ss);
+                            }
+                        }
+                        r = rsqrtf(ss / 128.0f + E.eps);
+                    }
+                    __nv_bfloat16 *dst0 = nullptr, *dst1 = nullptr;
+                    if (row_ok && n0 + hh * 128 < args.N) {
+                        if (is_q) {
+                            dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
+                        } else {
+                            const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
+                            dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
+                            const int page = E.pages[(size_t)slot * E.pages_per_seq + pos / 16];
+                            dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
+                                   ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + pos % 16) * 128;
+                        }
+                    }
+                    const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
+                        uint32_t lo[16], hi[16];
+                        ptx::tmem_ld16(t_head + c * 16, lo);
+                        ptx::tmem_ld16(t_head + 64 + c * 16, hi);
+                        ptx::tmem_ld_wait();
+                        float a[16], b[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            a[j] = has_k ? __uint_as_float(lo[j]) : 0.f;
+                            b[j] = has_k ? __uint_as_float(hi[j]) : 0.f;
+                        }
+                        if (rotate && dst0) {
+                            const float4 *cs4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)pos * 64 + 16 * c);
+                            const float4 *sn4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)pos * 64 + 16 * c);
+                            const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
+                            const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
+                            float cf[16], sf[16], wl[16], wh[16];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const float4 cv = cs4[q], sv = sn4[q];
+                                cf[4 * q] = cv.x; cf[4 * q + 1] = cv.y; cf[4 * q + 2] = cv.z; cf[4 * q + 3] = cv.w;
+                                sf[4 * q] = sv.x; sf[4 * q + 1] = sv.y; sf[4 * q + 2] = sv.z; sf[4 * q + 3] = sv.w;
+                            }
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) {
+                                const uint4 l = wl4[q], h = wh4[q];
+                                const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    wl[8 * q + 2 * e] = __uint_as_float(lw[e] << 16);
+                                    wl[8 * q + 2 * e + 1] = __uint_as_float(lw[e] & 0xFFFF0000u);
+                                    wh[8 * q + 2 * e] = __uint_as_float(hw[e] << 16);
+                                    wh[8 * q + 2 * e + 1] = __uint_as_float(hw[e] & 0xFFFF0000u);
+                                }
+                            }
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                const float x0 = a[j] * r * wl[j], x1 = b[j] * r * wh[j];
+                                a[j] = x0 * cf[j] - x1 * sf[j];
+                                b[j] = x1 * cf[j] + x0 * sf[j];
+                            }
+                        }
+                        if (dst0) {
+                            uint32_t pl[8], ph[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                pl[e] = pack_bf16(a[2 * e], a[2 * e + 1]);
+                                ph[e] = pack_bf16(b[2 * e], b[2 * e + 1]);
+                            }
+                            const uint4 l0 = make_uint4(pl[0], pl[1], pl[2], pl[3]), l1 = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+                            const uint4 h0 = make_uint4(ph[0], ph[1], ph[2], ph[3]), h1 = make_uint4(ph[4], ph[5], ph[6], ph[7]);
+                            uint4 *d0 = reinterpret_cast<uint4 *>(dst0 + 16 * c);
+                            uint4 *e0 = reinterpret_cast<uint4 *>(dst0 + 64 + 16 * c);
+                            d0[0] = l0; d0[1] = l1; e0[0] = h0; e0[1] = h1;
+                            if (dst1) {
+                                uint4 *d1 = reinterpret_cast<uint4 *>(dst1 + 16 * c);
+                                uint4 *e1 = reinterpret_cast<uint4 *>(dst1 + 64 + 16 * c);
+                                d1[0] = l0; d1[1] = l1; e1[0] = h0; e1[1] = h1;
+                            }
+                        }
+                    }
+                }
+            } else if (EPI == EPI_SWIGLU) {
                 for (int b = 0; b < BN / 128; ++b) {
 #pragma unroll 1
                     for (int j = 0; j < 4; ++j) {
@@ -385,6 +494,9 @@ cudaError_t launch_epi(const CUtensorMap &ta, const CUtensorMap &tb, const GemmA
         case EPI_SWIGLU: return launch_bn<BN, EPI_SWIGLU>(ta, tb, args, sms, stream);
         case EPI_PARTIAL: return launch_bn<BN, EPI_PARTIAL>(ta, tb, args, sms, stream);
         case EPI_BF16: return launch_bn<BN, EPI_BF16>(ta, tb, args, sms, stream);
+        case EPI_QKV:
+            if (BN >= 128) return launch_bn<BN, EPI_QKV>(ta, tb, args, sms, stream);
+            return cudaErrorInvalidValue;
     }
     return cudaErrorInvalidValue;
 }
@@ -407,6 +519,16 @@ const char *gemm_check(const GemmArgs &a) {
     if (a.epi == EPI_RESID && (a.ldr % 4 || ((uintptr_t)a.resid & 15))) return "resid needs 16-byte aligned rows";
     if (a.epi == EPI_BF16 && (a.ldo % 8 || ((uintptr_t)a.out_bf16 & 15))) return "bf16 output needs 16-byte rows";
     if (a.epi == EPI_PARTIAL && !a.partial) return "partial output missing";
+    if (a.epi == EPI_QKV) {
+        const QkvEpilogue &q = a.qkv;
+        if (a.bn < 128 || a.N % 128 || a.N != (q.q_heads + 2 * q.kv_heads) * 128)
+            return "the q/k/v epilogue needs bn >= 128 and N = (q_heads + 2 kv_heads) * 128";
+        if (!q.q_out || !q.k_out || !q.v_out || !q.pool || !q.pages || !q.q_norm || !q.k_norm || !q.cos_t ||
+            !q.sin_t || !q.tok_slot || !q.tok_pos)
+            return "the q/k/v epilogue is missing a pointer";
+        if (((uintptr_t)q.q_out | (uintptr_t)q.k_out | (uintptr_t)q.v_out | (uintptr_t)q.pool) & 15)
+            return "the q/k/v epilogue outputs must be 16-byte aligned";
+    }
     if (!a.err) return "error word missing";
     return nullptr;
 }

@@ -126,9 +126,11 @@ static int choose_splits(int m_tiles, int kb, int sms) {
 }
 
 static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, int K, int epi, int bn, int splits,
-                       void *out, int ldo, const float *resid, int ldr, size_t split_stride) {
+                       void *out, int ldo, const float *resid, int ldr, size_t split_stride,
+                       const QkvEpilogue *qkv = nullptr) {
     GemmArgs a;
     memset(&a, 0, sizeof a);
+    if (qkv) a.qkv = *qkv;
     a.M = M;
     a.N = N;
     a.K = K;
@@ -517,26 +519,24 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
          "embed_norm");
     for (int l = 0; l < c.layers; ++l) {
         const Layer &L = Q->layers[l];
-        LTRY(gemm(Q, Q->xn, L.w_qkv, T, Q->qkv_rows, H, EPI_F32, 256, 1, Q->qkv, Q->qkv_rows, nullptr, 0, 0));
-        QkvArgs qa;
-        qa.qkv = Q->qkv;
-        qa.splits = 1;
-        qa.split_stride = 0;
-        qa.T = T;
-        qa.q_heads = qh;
-        qa.kv_heads = kvh;
-        qa.q_norm = L.q_norm;
-        qa.k_norm = L.k_norm;
-        qa.eps = c.eps;
-        qa.cos_t = Q->cos_t;
-        qa.sin_t = Q->sin_t;
-        qa.tok_slot = Q->tok_slot;
-        qa.tok_pos = Q->tok_pos;
-        qa.kv = KvLayout{Q->pool + (size_t)l * Q->layer_pool_elems, Q->d_pages, Q->maxp, kvh};
-        qa.q_out = Q->q;
-        qa.k_out = Q->k;
-        qa.v_out = Q->v;
-        KTRY(Q, launch_qk_norm_rope_kv(qa, st), "qk_norm_rope_kv");
+        // q/k/v GEMM with QK-RMSNorm, RoPE and the paged KV append in its epilogue (no fp32 q/k/v round trip).
+        QkvEpilogue qe;
+        qe.q_out = Q->q;
+        qe.k_out = Q->k;
+        qe.v_out = Q->v;
+        qe.pool = Q->pool + (size_t)l * Q->layer_pool_elems;
+        qe.pages = Q->d_pages;
+        qe.pages_per_seq = Q->maxp;
+        qe.q_heads = qh;
+        qe.kv_heads = kvh;
+        qe.q_norm = L.q_norm;
+        qe.k_norm = L.k_norm;
+        qe.eps = c.eps;
+        qe.cos_t = Q->cos_t;
+        qe.sin_t = Q->sin_t;
+        qe.tok_slot = Q->tok_slot;
+        qe.tok_pos = Q->tok_pos;
+        LTRY(gemm(Q, Q->xn, L.w_qkv, T, Q->qkv_rows, H, EPI_QKV, 256, 1, nullptr, Q->qkv_rows, nullptr, 0, 0, &qe));
         PrefillAttnArgs pa;
         pa.q = Q->q;
         pa.k = Q->k;

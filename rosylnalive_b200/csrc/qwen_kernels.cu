@@ -120,6 +120,31 @@ __global__ void __launch_bounds__(256) resid_norm_kernel(float *x, const float *
     }
 }
 
+// Prefill form (no split partials): one warp per row, 8 rows per block, the row's float4s spread over the lanes and a
+// shuffle reduction, so the many short rows of a prefill do not pay a block-wide barrier each.
+__global__ void __launch_bounds__(256) norm_rows_warp_kernel(const float *x, int T, int hidden,
+                                                             const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * hidden);
+    const int n4 = hidden / 4;
+    float ss = 0.f;
+    for (int c = lane; c < n4; c += 32) {
+        const float4 v = xr[c];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    const float r = rsqrtf(warp_sum(ss) / hidden + eps);
+    for (int c = lane; c < n4; c += 32) {
+        const float4 v = xr[c];
+        const uint2 wv = *reinterpret_cast<const uint2 *>(w + 4 * c);
+        *reinterpret_cast<uint2 *>(xn + (size_t)row * hidden + 4 * c) =
+            pack4(v.x * r * __uint_as_float(wv.x << 16), v.y * r * __uint_as_float(wv.x & 0xFFFF0000u),
+                  v.z * r * __uint_as_float(wv.y << 16), v.w * r * __uint_as_float(wv.y & 0xFFFF0000u));
+    }
+}
+
 // ---- q/k norm + RoPE + KV append --------------------------------------------------------------------------------
 
 // One warp per (token, head row); lane l owns dims 4l..4l+3. Head rows 0..q-1 are q, then kv k rows, then kv v rows.
@@ -491,6 +516,9 @@ cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *e
 
 cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
                               const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st) {
+    if (splits == 0)
+        return launch_kernel(norm_rows_warp_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float *)x, T, hidden,
+                             w, eps, xn);
     return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, partial, splits, split_stride, hidden, w,
                          eps, xn);
 }
