@@ -193,11 +193,12 @@ lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *desc);
 
 /* Causal GQA attention of packed sequences (each starting at position 0), bf16 in/out, fp32 softmax and
  * accumulation: q [T, q_heads, 128], k/v [T, kv_heads, 128] (K after QK-norm and RoPE), cu_seqlens int32 [nseq + 1]
- * (device), out [T, q_heads, 128]. Replaces the reference's attention_gqa_causal
+ * (device, cu_seqlens[nseq] = total_tokens = T), out [T, q_heads, 128]. Runs on the tcgen05 tensor cores (TMA tiles,
+ * TMEM accumulators). Replaces the reference's attention_gqa_causal
  * (src/Lrm.Shaders/hlsl/kernels/attention/attention_gqa_causal.hlsl) for prefill on the bf16 path. */
 typedef struct lrm_prefill_attn_desc {
     uint64_t q, k, v, out, cu_seqlens;
-    int32_t nseq, max_len, q_heads, kv_heads, head_dim;
+    int32_t nseq, max_len, q_heads, kv_heads, head_dim, total_tokens;
     float scale;
 } lrm_prefill_attn_desc;
 lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *desc);

@@ -29,6 +29,7 @@ SOURCES = [
     "gemm_tcgen05.cu",
     "qwen_kernels.cu",
     "flash_prefill.cu",
+    "flash_tc.cu",
     "qwen_engine.cu",
     "decode_attn_static.cu",
 ]

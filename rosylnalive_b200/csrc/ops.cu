@@ -134,7 +134,9 @@ lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d
         return op_fail(LRM_ERR_ARGUMENT, "prefill attention: bad sizes (kv_heads must divide q_heads)");
     if (!d->q || !d->k || !d->v || !d->out || !d->cu_seqlens || ((d->q | d->k | d->v | d->out) & 15))
         return op_fail(LRM_ERR_ARGUMENT, "prefill attention: pointers must be non-null and 16-byte aligned");
-    if (!device_error_word()) return LRM_ERR_CUDA;
+    if (d->total_tokens < 1) return op_fail(LRM_ERR_ARGUMENT, "prefill attention: total_tokens must be positive");
+    uint32_t *err = device_error_word();
+    if (!err) return LRM_ERR_CUDA;
     PrefillAttnArgs a;
     a.q = (const __nv_bfloat16 *)d->q;
     a.k = (const __nv_bfloat16 *)d->k;
@@ -146,7 +148,7 @@ lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d
     a.q_heads = d->q_heads;
     a.kv_heads = d->kv_heads;
     a.scale_log2 = d->scale * 1.4426950408889634f;
-    return op_cuda(launch_prefill_attention(a, (cudaStream_t)stream), "prefill attention");
+    return op_cuda(launch_prefill_attention_tc(a, d->total_tokens, err, (cudaStream_t)stream), "prefill attention");
 }
 
 uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int32_t pages_per_seq,

@@ -125,8 +125,9 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
 
 // Instruction descriptor of kind::f16 with bf16 A and B (both K-major), fp32 accumulation, shape M x N:
 // c_format F32 = 1 (bits 4-5), a_format BF16 = 1 (7-9), b_format BF16 = 1 (10-12), N >> 3 (17-22), M >> 4 (24-28).
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t M, uint32_t N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+// With b_mn_major, B is MN-major (b_major, bit 16): B rows hold consecutive N elements for one k.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t M, uint32_t N, bool b_mn_major = false) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn_major ? (1u << 16) : 0u) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, issued by one thread.
@@ -155,6 +156,40 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// The store counterpart: thread i writes lane (base lane + i), columns col..col+15.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 3D tiled load of box {x, y, z} at coordinates (x, y, z) (x innermost), completing tx bytes on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *smem, const CUtensorMap *map, uint64_t *bar, int32_t x, int32_t y,
+                                            int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(smem_u32(smem)),
+        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// Shared-memory descriptor for an MN-major operand stored with the 128-byte swizzle: rows of 128 bytes hold 64
+// consecutive MN elements for one k, 8 k-rows form a 1024-byte atom; `lbo` is the byte distance between 64-element
+// MN chunks and `sbo` the distance between 8-row k groups (bits as in sw128_kmajor_desc).
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
 
 // Programmatic dependent launch. A kernel launched with programmatic stream serialization may start before the
 // previous kernel in the stream has finished: griddep_wait blocks until that kernel has completed and its memory is

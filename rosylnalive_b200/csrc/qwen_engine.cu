@@ -548,7 +548,7 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         pa.q_heads = qh;
         pa.kv_heads = kvh;
         pa.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
-        KTRY(Q, launch_prefill_attention(pa, st), "prefill_attention");
+        KTRY(Q, launch_prefill_attention_tc(pa, T, Q->err, st), "prefill_attention");
         LTRY(gemm(Q, Q->attn, L.w_o, T, H, qh * kHeadDim, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
         KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, L.post_norm, c.eps, Q->xn, st), "resid_norm");
         LTRY(gemm(Q, Q->xn, L.w_gu, T, 2 * I, H, EPI_SWIGLU, 256, 1, Q->act, I, nullptr, 0, 0));

@@ -21,7 +21,8 @@ class GemmDesc(ctypes.Structure):
 
 class PrefillAttnDesc(ctypes.Structure):
     _fields_ = [("q", U64), ("k", U64), ("v", U64), ("out", U64), ("cu_seqlens", U64), ("nseq", I32),
-                ("max_len", I32), ("q_heads", I32), ("kv_heads", I32), ("head_dim", I32), ("scale", ctypes.c_float)]
+                ("max_len", I32), ("q_heads", I32), ("kv_heads", I32), ("head_dim", I32), ("total_tokens", I32),
+                ("scale", ctypes.c_float)]
 
 
 class DecodeAttnDesc(ctypes.Structure):
@@ -76,7 +77,7 @@ def gemm(a, b, out, epilogue=GEMM_F32, resid=None, splits=1, bn=0, ldo=None, spl
 def prefill_attention(q, k, v, out, cu_seqlens, max_len, scale, stream=None):
     """Causal GQA attention of packed sequences: q [T, qh, 128], k/v [T, kvh, 128], cu_seqlens int32 [nseq + 1]."""
     d = PrefillAttnDesc(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), cu_seqlens.data_ptr(),
-                        cu_seqlens.numel() - 1, max_len, q.shape[1], k.shape[1], q.shape[2], scale)
+                        cu_seqlens.numel() - 1, max_len, q.shape[1], k.shape[1], q.shape[2], q.shape[0], scale)
     N.check(N.lib().lrm_op_prefill_attention(_stream(stream), ctypes.byref(d)), None, "prefill_attention")
 
 
