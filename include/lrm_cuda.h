@@ -188,6 +188,8 @@ typedef struct lrm_gemm_desc {
     uint64_t resid;   /* RESID: fp32 [m, ldr] */
     int32_t ldr;
     uint64_t split_stride; /* PARTIAL: elements between split slices */
+    int32_t cta_pair;      /* 0 chooses; 1 one CTA per 128-row tile; 2 two-SM clusters sharing 256 x 256 tiles
+                              (tcgen05 cta_group::2; needs bn 256, one split, not PARTIAL) */
 } lrm_gemm_desc;
 lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *desc);
 

@@ -28,7 +28,6 @@ SOURCES = [
     "ops.cu",
     "gemm_tcgen05.cu",
     "qwen_kernels.cu",
-    "flash_prefill.cu",
     "flash_tc.cu",
     "qwen_engine.cu",
     "decode_attn_static.cu",

@@ -1,18 +1,22 @@
 // flash_tc.cu -- causal GQA prefill attention on the 5th-generation tensor cores (tcgen05, TMEM, TMA).
 //
-// One CTA owns 128 query rows of one head (rows of packed sequences, each starting at position 0) and walks the
-// 128-key tiles up to the causal limit:
-//   warp 0      TMA producer: Q once, then K and V tiles (3D tensor maps over [tokens][heads][128], 128-byte
-//               swizzle, boxes of 64 dims x 128 rows) into a 2-stage ring;
-//   warp 1      tensor-core issuer (one thread): S_j = Q K_j^T into one of two TMEM accumulators (128 x 128 fp32), and
-//               O += P_j V_j into a third, with P from shared memory (K-major) and V read MN-major straight from its
-//               [key][dim] tile (no transpose);
-//   warps 2..5  softmax: thread = query row (its TMEM lane). Pass 1 reads the row of S for the tile maximum, pass 2
-//               reads it again, writes P = exp2(S * scale * log2 e - m) as bf16 into the swizzled P tile and adds to
-//               the row sum. The running maximum m only moves when a tile's maximum exceeds it by more than 8 (a
-//               factor 256 in P); then O is rescaled in TMEM (tcgen05.ld / st) while the tensor core is idle on it.
-//               At the end O / l is written as bf16.
-// QK_{j+1} runs while the softmax of tile j runs. Every mbarrier wait is bounded and reports to the error word.
+// One CTA owns 128 query rows of up to two query heads that share a KV head (two "slots"; one when the group size
+// q_heads / kv_heads is odd), so every K/V tile is loaded once for both, and walks the 128-key tiles up to the causal
+// limit. Tensor memory (512 columns) holds per slot S (128 x 128 fp32) and O (128 x 128 fp32); P overwrites S in
+// place as bf16 and the P V product reads it from tensor memory, so P never goes through shared memory.
+//   warp 0      TMA producer: Q of both slots once, then K and V tiles (3D tensor maps over [tokens][heads][128],
+//               128-byte swizzle, boxes of 64 dims x 128 rows) into a 2-stage ring with separate K and V barriers;
+//   warp 1      tensor-core issuer (one thread), per key tile j: S_s = Q_s K_j^T for both slots, then
+//               O_s += P_s V_j (V read MN-major straight from its [key][dim] tile). S_s of tile j+1 is only issued
+//               once P_s V_j has completed, since it overwrites P_s;
+//   warps 4..11 softmax, one warpgroup per slot, thread = query row (its TMEM lane): the row of S comes into
+//               registers in one go, keys past the row or the sequence are masked (diagonal and tail tiles only),
+//               P = 2^(S * scale * log2 e - m) is written back as bf16 and summed in fp32. The reference maximum m
+//               only moves when a tile's maximum exceeds it by more than 8 (a factor 256 in P); then O is rescaled
+//               in tensor memory, which is safe there because S_j completing implies P V_{j-1} has. At the end O / l
+//               is written as bf16.
+// While one slot's softmax runs, the tensor core works on the other slot. Every mbarrier wait is bounded and
+// reports to the error word.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -26,17 +30,20 @@
 namespace lrm {
 namespace {
 
-constexpr int TQ = 128, TK = 128, ST = 2;
+constexpr int TQ = 128, TK = 128, ST = 2, SLOTS = 2;
 constexpr int SUB = 128 * 64 * 2;  // one [128 rows][64] bf16 swizzled sub-tile
 constexpr int TILE = 2 * SUB;      // [128 rows][128]
-constexpr int SMEM_BYTES = TILE + ST * 2 * TILE + TILE + 1024 + 256;
-constexpr int kThreads = 192;
+constexpr int SMEM_BYTES = SLOTS * TILE + ST * 2 * TILE + 1024 + 256;
+constexpr int kThreads = 384;      // warpgroup 0: producer, issuer (two warps idle); warpgroups 1, 2: softmax
+constexpr int kRegsLaunch = 168;    // 65536 / 384, rounded down to the allocation unit of 8
+constexpr int kRegsControl = 56, kRegsSoftmax = 216;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split exceeds the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct FlashTcParams {
     const int32_t *cu_seqlens;
     __nv_bfloat16 *out;
-    int nseq, max_len, q_heads, kv_heads;
+    int nseq, max_len, q_heads, kv_heads, heads_per_cta;
     float scale_log2;
     uint32_t *err;
 };
@@ -52,29 +59,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::griddep_wait();
     ptx::griddep_launch();
     const int n_qt = (p.max_len + TQ - 1) / TQ;
-    const int qt = n_qt - 1 - (int)blockIdx.x;  // the longest rows first
-    const int h = blockIdx.y, seq = blockIdx.z;
+    const int qt = n_qt - 1 - (int)blockIdx.z;  // the longest query tiles of every head and sequence first
+    const int h0 = blockIdx.x * p.heads_per_cta, seq = blockIdx.y;
+    const int nslots = p.heads_per_cta;
     const int start = p.cu_seqlens[seq];
     const int len = p.cu_seqlens[seq + 1] - start;
     const int q0 = qt * TQ;
     if (q0 >= len) return;  // whole CTA, before any barrier or TMEM use
-    const int kvh = h / (p.q_heads / p.kv_heads);
+    const int kvh = h0 / (p.q_heads / p.kv_heads);
     const int n_kt = (min(len, q0 + TQ) - 1) / TK + 1;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sQ = smem;
-    uint8_t *sK = sQ + TILE;            // ST tiles
+    uint8_t *sQ = smem;                 // SLOTS tiles
+    uint8_t *sK = sQ + SLOTS * TILE;    // ST tiles
     uint8_t *sV = sK + ST * TILE;       // ST tiles
-    uint8_t *sP = sV + ST * TILE;
-    uint64_t *bars = (uint64_t *)(sP + TILE);
+    uint64_t *bars = (uint64_t *)(sV + ST * TILE);
     uint64_t *q_full = bars;
-    uint64_t *kv_full = bars + 1;       // ST
-    uint64_t *kv_empty = kv_full + ST;  // ST
-    uint64_t *s_full = kv_empty + ST;   // 2
-    uint64_t *p_full = s_full + 2;
-    uint64_t *o_done = p_full + 1;
-    uint64_t *fin = o_done + 1;
+    uint64_t *k_full = q_full + 1;      // ST
+    uint64_t *v_full = k_full + ST;     // ST
+    uint64_t *kv_empty = v_full + ST;   // ST
+    uint64_t *s_full = kv_empty + ST;   // SLOTS
+    uint64_t *p_full = s_full + SLOTS;  // SLOTS
+    uint64_t *pv_done = p_full + SLOTS; // SLOTS
+    uint64_t *fin = pv_done + SLOTS;
     uint32_t *tmem_slot = (uint32_t *)(fin + 1);
     uint32_t *err = p.err;
 
@@ -82,13 +90,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         ptx::mbar_init(q_full, 1);
         for (int s = 0; s < ST; ++s) {
-            ptx::mbar_init(&kv_full[s], 1);
+            ptx::mbar_init(&k_full[s], 1);
+            ptx::mbar_init(&v_full[s], 1);
             ptx::mbar_init(&kv_empty[s], 1);
         }
-        ptx::mbar_init(&s_full[0], 1);
-        ptx::mbar_init(&s_full[1], 1);
-        ptx::mbar_init(p_full, 4);
-        ptx::mbar_init(o_done, 1);
+        for (int s = 0; s < SLOTS; ++s) {
+            ptx::mbar_init(&s_full[s], 1);
+            ptx::mbar_init(&p_full[s], 4);
+            ptx::mbar_init(&pv_done[s], 1);
+        }
         ptx::mbar_init(fin, 1);
         ptx::fence_barrier_init();
         ptx::prefetch_tmap(&tq);
@@ -103,168 +113,183 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS[2] = {tmem, tmem + 128};
-    const uint32_t tO = tmem + 256;
-
-    if (warp == 0) {
-        if (ptx::elect_one()) {
-            ptx::mbar_arrive_expect_tx(q_full, TILE);
-            ptx::tma_load_3d(sQ, &tq, q_full, 0, h, start + q0);
-            ptx::tma_load_3d(sQ + SUB, &tq, q_full, 64, h, start + q0);
-            int j = 0;
-            for (; j < n_kt; ++j) {
-                const int s = j % ST;
-                if (!ptx::mbar_wait(&kv_empty[s], ((j / ST) & 1) ^ 1, err, 0x3001)) break;
-                ptx::mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
-                const int rows = start + j * TK;
-                ptx::tma_load_3d(sK + s * TILE, &tk, &kv_full[s], 0, kvh, rows);
-                ptx::tma_load_3d(sK + s * TILE + SUB, &tk, &kv_full[s], 64, kvh, rows);
-                ptx::tma_load_3d(sV + s * TILE, &tv, &kv_full[s], 0, kvh, rows);
-                ptx::tma_load_3d(sV + s * TILE + SUB, &tv, &kv_full[s], 64, kvh, rows);
-            }
-            ptx::mbar_wait(q_full, 0, err, 0x3002);
-            for (int i = j > ST ? j - ST : 0; i < j; ++i) ptx::mbar_wait(&kv_full[i % ST], (i / ST) & 1, err, 0x3002);
-        }
-    } else if (warp == 1) {
-        if (ptx::elect_one()) {
-            constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(128, 128, false);
-            constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(128, 128, true);
-            const uint32_t aQ = ptx::smem_u32(sQ), aP = ptx::smem_u32(sP);
-            bool ok = ptx::mbar_wait(q_full, 0, err, 0x3003);
-            auto issue_qk = [&](int j) -> bool {
-                const int s = j % ST;
-                if (!ptx::mbar_wait(&kv_full[s], (j / ST) & 1, err, 0x3004)) return false;
-                ptx::tc_fence_after();
-                const uint32_t aK = ptx::smem_u32(sK + s * TILE);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
-                    ptx::mma_bf16(tS[j & 1], ptx::sw128_kmajor_desc(aQ + off), ptx::sw128_kmajor_desc(aK + off),
-                                  idesc_qk, kk > 0 ? 1u : 0u);
+    // slot s: S at columns 256 s, O at 256 s + 128
+    if (warp < 4) {
+        ptx::setmaxnreg_dec<kRegsControl>();
+        if (warp == 0) {
+            if (ptx::elect_one()) {
+                ptx::mbar_arrive_expect_tx(q_full, nslots * TILE);
+                for (int s = 0; s < nslots; ++s) {
+                    ptx::tma_load_3d(sQ + s * TILE, &tq, q_full, 0, h0 + s, start + q0);
+                    ptx::tma_load_3d(sQ + s * TILE + SUB, &tq, q_full, 64, h0 + s, start + q0);
                 }
-                ptx::mma_commit(&s_full[j & 1]);
-                return true;
-            };
-            if (ok) ok = issue_qk(0);
-            for (int j = 0; ok && j < n_kt; ++j) {
-                if (j + 1 < n_kt && !issue_qk(j + 1)) break;
-                if (!ptx::mbar_wait(p_full, j & 1, err, 0x3005)) break;
-                ptx::tc_fence_after();
-                const uint32_t aV = ptx::smem_u32(sV + (j % ST) * TILE);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t da = ptx::sw128_kmajor_desc(aP + (kk >> 2) * SUB + (kk & 3) * 32);
-                    const uint64_t db = ptx::sw128_mnmajor_desc(aV + kk * 2048, SUB, 1024);
-                    ptx::mma_bf16(tO, da, db, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                int j = 0;
+                for (; j < n_kt; ++j) {
+                    const int s = j % ST;
+                    if (!ptx::mbar_wait(&kv_empty[s], ((j / ST) & 1) ^ 1, err, 0x3001)) break;
+                    const int rows = start + j * TK;
+                    ptx::mbar_arrive_expect_tx(&k_full[s], TILE);
+                    ptx::tma_load_3d(sK + s * TILE, &tk, &k_full[s], 0, kvh, rows);
+                    ptx::tma_load_3d(sK + s * TILE + SUB, &tk, &k_full[s], 64, kvh, rows);
+                    ptx::mbar_arrive_expect_tx(&v_full[s], TILE);
+                    ptx::tma_load_3d(sV + s * TILE, &tv, &v_full[s], 0, kvh, rows);
+                    ptx::tma_load_3d(sV + s * TILE + SUB, &tv, &v_full[s], 64, kvh, rows);
                 }
-                ptx::mma_commit(&kv_empty[j % ST]);
-                ptx::mma_commit(o_done);
+                // Our own copies in flight must land before the CTA exits (this matters on the error path).
+                ptx::mbar_wait(q_full, 0, err, 0x3002);
+                for (int i = j > ST ? j - ST : 0; i < j; ++i) {
+                    ptx::mbar_wait(&k_full[i % ST], (i / ST) & 1, err, 0x3002);
+                    ptx::mbar_wait(&v_full[i % ST], (i / ST) & 1, err, 0x3002);
+                }
             }
-            // No MMA may still be writing TMEM when it is freed (this matters on the error path).
-            ptx::mma_commit(fin);
-            ptx::mbar_wait(fin, 0, err, 0x3009);
+        } else if (warp == 1) {
+            if (ptx::elect_one()) {
+                constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(128, 128, false);
+                constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(128, 128, true);
+                bool ok = ptx::mbar_wait(q_full, 0, err, 0x3003);
+                for (int j = 0; ok && j < n_kt; ++j) {
+                    const int st = j % ST;
+                    if (!ptx::mbar_wait(&k_full[st], (j / ST) & 1, err, 0x3004)) break;
+                    const uint32_t aK = ptx::smem_u32(sK + st * TILE);
+                    for (int s = 0; s < nslots && ok; ++s) {
+                        // S_s of this tile overwrites P_s of the previous one: P_s V_{j-1} must have completed.
+                        if (j > 0 && !ptx::mbar_wait(&pv_done[s], (j - 1) & 1, err, 0x3005)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        const uint32_t aQ = ptx::smem_u32(sQ + s * TILE);
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
+                            ptx::mma_bf16(tmem + 256 * s, ptx::sw128_kmajor_desc(aQ + off),
+                                          ptx::sw128_kmajor_desc(aK + off), idesc_qk, kk > 0 ? 1u : 0u);
+                        }
+                        ptx::mma_commit(&s_full[s]);
+                    }
+                    if (!ok || !ptx::mbar_wait(&v_full[st], (j / ST) & 1, err, 0x3004)) break;
+                    const uint32_t aV = ptx::smem_u32(sV + st * TILE);
+                    for (int s = 0; s < nslots; ++s) {
+                        if (!ptx::mbar_wait(&p_full[s], j & 1, err, 0x3006)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint64_t db = ptx::sw128_mnmajor_desc(aV + kk * 2048, SUB, 1024);
+                            ptx::mma_bf16_ts(tmem + 256 * s + 128, tmem + 256 * s + kk * 8, db, idesc_pv,
+                                             (j > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        ptx::mma_commit(&pv_done[s]);
+                    }
+                    ptx::mma_commit(&kv_empty[st]);
+                }
+                // No MMA may still be writing TMEM when it is freed (this matters on the error path).
+                ptx::mma_commit(fin);
+                ptx::mbar_wait(fin, 0, err, 0x3009);
+            }
         }
     } else {
-        const int q = warp & 3;
-        const int rl = q * 32 + lane;  // row within the tile
-        const int row = q0 + rl;       // query position within the sequence
-        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        float m_ref = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < n_kt && ok; ++j) {
-            if (!ptx::mbar_wait(&s_full[j & 1], (j >> 1) & 1, err, 0x3006)) {
-                ok = false;
-                break;
-            }
-            ptx::tc_fence_after();
-            const uint32_t ts = tS[j & 1] + lane_off;
-            const int key0 = j * TK;
-            // pass 1: the tile maximum of this row (masked keys: beyond the row, or beyond the sequence)
-            float tmax = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < 8; c += 2) {
-                uint32_t u0[16], u1[16];
-                ptx::tmem_ld16(ts + c * 16, u0);
-                ptx::tmem_ld16(ts + c * 16 + 16, u1);
+        ptx::setmaxnreg_inc<kRegsSoftmax>();
+        if (warp - 4 < 4 * nslots) {
+            const int s = (warp - 4) >> 2;
+            const int q = warp & 3;  // TMEM lane quarter this warp may access
+            const int rl = q * 32 + lane;
+            const int row = q0 + rl;  // query position within the sequence
+            const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+            const uint32_t tS = tmem + 256 * s + lane_off, tO = tS + 128;
+            const float sc = p.scale_log2;
+            float m_ref = -INFINITY, l = 0.f;
+            bool ok = true;
+            for (int j = 0; j < n_kt; ++j) {
+                if (!ptx::mbar_wait(&s_full[s], j & 1, err, 0x3007)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                float x[128];
+                ptx::tmem_ld32(tS, reinterpret_cast<uint32_t *>(x));
+                ptx::tmem_ld32(tS + 32, reinterpret_cast<uint32_t *>(x) + 32);
+                ptx::tmem_ld32(tS + 64, reinterpret_cast<uint32_t *>(x) + 64);
+                ptx::tmem_ld32(tS + 96, reinterpret_cast<uint32_t *>(x) + 96);
                 ptx::tmem_ld_wait();
+                const int key0 = j * TK;
+                // Masking is needed when some key of the tile lies past the warp's first row or past the sequence.
+                if (key0 + TK - 1 > q0 + q * 32 || key0 + TK > len) {
+                    const int lim = min(row - key0, len - 1 - key0);  // keys 0..lim of the tile are visible
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int k0 = key0 + c * 16 + e, k1 = k0 + 16;
-                    if (k0 <= row && k0 < len) tmax = fmaxf(tmax, __uint_as_float(u0[e]) * p.scale_log2);
-                    if (k1 <= row && k1 < len) tmax = fmaxf(tmax, __uint_as_float(u1[e]) * p.scale_log2);
+                    for (int e = 0; e < 128; ++e) x[e] = e <= lim ? x[e] : -INFINITY;
                 }
-            }
-            float alpha = 1.f;
-            bool rescale = false;
-            if (j == 0) {
-                m_ref = tmax;
-            } else if (tmax > m_ref + kRescaleThreshold) {
-                alpha = exp2f(m_ref - tmax);
-                m_ref = tmax;
-                rescale = true;
-            }
-            // P_{j-1} V_{j-1} must be done before P is overwritten or O is rescaled.
-            if (j > 0 && !ptx::mbar_wait(o_done, (j - 1) & 1, err, 0x3007)) {
-                ok = false;
-                break;
-            }
-            ptx::tc_fence_after();
-            if (__any_sync(0xffffffffu, rescale)) {
-                l *= alpha;
+                float mx[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx[e] = fmaxf(x[e], x[e + 8]);
+#pragma unroll
+                for (int e = 16; e < 128; e += 8) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], x[e + u]);
+                }
+                const float tmax =
+                    fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+                    sc;
+                bool rescale = false;
+                float alpha = 1.f;
+                if (j == 0) {
+                    m_ref = tmax;
+                } else if (tmax > m_ref + kRescaleThreshold) {
+                    alpha = ptx::ex2(m_ref - tmax);
+                    m_ref = tmax;
+                    rescale = true;
+                }
+                if (__any_sync(0xffffffffu, rescale)) {
+                    // S_j has completed, so P V_{j-1} (issued before it) has too: O is quiescent.
+                    l *= alpha;
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t u[16];
-                    ptx::tmem_ld16(tO + lane_off + c * 16, u);
-                    ptx::tmem_ld_wait();
+                    for (int c = 0; c < 128; c += 32) {
+                        uint32_t u[32];
+                        ptx::tmem_ld32(tO + c, u);
+                        ptx::tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-                    ptx::tmem_st16(tO + lane_off + c * 16, u);
+                        for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+                        ptx::tmem_st32(tO + c, u);
+                    }
                 }
+                const float nm = -m_ref;
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t pk[64];
+#pragma unroll
+                for (int e = 0; e < 64; ++e) {
+                    const float a = ptx::ex2(fmaf(x[2 * e], sc, nm));
+                    const float b = ptx::ex2(fmaf(x[2 * e + 1], sc, nm));
+                    ls[e & 3] += a + b;
+                    pk[e] = pack2(a, b);
+                }
+                l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                ptx::tmem_st32(tS, pk);
+                ptx::tmem_st32(tS + 32, pk + 32);
                 ptx::tmem_st_wait();
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&p_full[s]);
             }
-            // pass 2: P = exp2(s - m_ref) as bf16 into the swizzled P tile (K-major, two 64-key sub-tiles)
+            if (ok && ptx::mbar_wait(&pv_done[s], (n_kt - 1) & 1, err, 0x3008)) {
+                ptx::tc_fence_after();
+                const float inv = 1.f / l;
+                __nv_bfloat16 *dst = p.out + ((size_t)(start + row) * p.q_heads + h0 + s) * kHeadDim;
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                uint32_t u[16];
-                ptx::tmem_ld16(ts + c * 16, u);
-                ptx::tmem_ld_wait();
-                float pv[16];
+                for (int c = 0; c < 128; c += 32) {
+                    uint32_t u[32];
+                    ptx::tmem_ld32(tO + c, u);
+                    ptx::tmem_ld_wait();
+                    if (row < len) {
+                        uint32_t w[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int key = key0 + c * 16 + e;
-                    pv[e] = (key <= row && key < len) ? exp2f(__uint_as_float(u[e]) * p.scale_log2 - m_ref) : 0.f;
-                    l += pv[e];
-                }
-                uint32_t w[8];
+                        for (int e = 0; e < 16; ++e)
+                            w[e] = pack2(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
+                        uint4 *d4 = reinterpret_cast<uint4 *>(dst + c);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) w[e] = pack2(pv[2 * e], pv[2 * e + 1]);
-                const int sub = c >> 2, chunk = (c & 3) * 2;
-                uint8_t *prow = sP + sub * SUB + rl * 128;
-                *reinterpret_cast<uint4 *>(prow + (((chunk) ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4 *>(prow + (((chunk + 1) ^ (rl & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
-            }
-            ptx::fence_proxy_async();
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(p_full);
-        }
-        if (ok && ptx::mbar_wait(o_done, (n_kt - 1) & 1, err, 0x3008)) {
-            ptx::tc_fence_after();
-            const float inv = 1.f / l;
-            __nv_bfloat16 *dst = p.out + ((size_t)(start + row) * p.q_heads + h) * kHeadDim;
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                uint32_t u[16];
-                ptx::tmem_ld16(tO + lane_off + c * 16, u);
-                ptx::tmem_ld_wait();
-                if (row < len) {
-                    uint32_t w[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        w[e] = pack2(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
-                    uint4 *d4 = reinterpret_cast<uint4 *>(dst + c * 16);
-                    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+                    }
                 }
             }
         }
@@ -326,9 +351,10 @@ cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_toke
     p.max_len = a.max_len;
     p.q_heads = a.q_heads;
     p.kv_heads = a.kv_heads;
+    p.heads_per_cta = ((a.q_heads / a.kv_heads) % 2 == 0) ? 2 : 1;
     p.scale_log2 = a.scale_log2;
     p.err = err;
-    dim3 grid((a.max_len + TQ - 1) / TQ, a.q_heads, a.nseq);
+    dim3 grid(a.q_heads / p.heads_per_cta, a.nseq, (a.max_len + TQ - 1) / TQ);
     return launch_kernel(flash_tc_kernel, grid, dim3(kThreads), SMEM_BYTES, st, tq, tk, tv, p);
 }
 

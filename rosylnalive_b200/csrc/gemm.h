@@ -45,11 +45,16 @@ struct GemmArgs {
     // first k-blocks are prefetched before the kernel waits for the previous one (decode: the weights).
     int independent;
     QkvEpilogue qkv;  // EPI_QKV only
+    // 0 chooses; 1 one CTA per 128 x bn tile; 2 pairs of CTAs (a cluster of two SMs) sharing 256 x 256 tiles through
+    // tcgen05 cta_group::2 MMAs (bn 256, one split, not EPI_PARTIAL).
+    int cta_pair;
 };
 
 // nullptr when the arguments are valid, else the reason.
 const char *gemm_check(const GemmArgs &a);
 // Encodes the tensor maps and launches the persistent kernel on `sms` CTAs at most.
 cudaError_t gemm_launch(const GemmArgs &a, int sms, cudaStream_t stream);
+// Whether gemm_launch runs `a` on CTA pairs.
+bool gemm_uses_pair(const GemmArgs &a);
 
 }  // namespace lrm

@@ -60,6 +60,213 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
+// The epilogue of one accumulator row (thread = TMEM lane): row `row` of the output, columns n0..n0+BN-1, read
+// from tensor memory at t_row (the row's lane, the accumulator's first column). has_k is false for an empty k
+// range (the accumulator is then treated as zero).
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_row, int row, int n0, bool has_k,
+                                              int split) {
+    if (EPI == EPI_QKV) {
+        // Two light passes over TMEM per 128-column head: the sum of squares, then the RoPE pairs (i, i + 64)
+        // sixteen at a time, normalised, rotated, rounded to bf16 and stored; few registers, vector loads.
+        const QkvEpilogue &E = args.qkv;
+        const bool row_ok = row < args.M;
+        const int pos = row_ok ? E.tok_pos[row] : 0;
+        const int slot = row_ok ? E.tok_slot[row] : 0;
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 128; ++hh) {
+            const uint32_t t_head = t_row + hh * 128;
+            const int head_row = (n0 + hh * 128) / 128;
+            const bool is_q = head_row < E.q_heads, is_k = !is_q && head_row < E.q_heads + E.kv_heads;
+            const bool rotate = is_q || is_k;
+            float r = 1.f;
+            if (rotate) {
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 8; c += 2) {
+                    uint32_t u0[16], u1[16];
+                    ptx::tmem_ld16(t_head + c * 16, u0);
+                    ptx::tmem_ld16(t_head + c * 16 + 16, u1);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float a = __uint_as_float(u0[j]), b = __uint_as_float(u1[j]);
+                        ss = fmaf(a, a, ss);
+                        ss = fmaf(b, b, ss);
+                    }
+                }
+                r = rsqrtf(ss / 128.0f + E.eps);
+            }
+            __nv_bfloat16 *dst0 = nullptr, *dst1 = nullptr;
+            if (row_ok && n0 + hh * 128 < args.N) {
+                if (is_q) {
+                    dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
+                } else {
+                    const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
+                    dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
+                    const int page = E.pages[(size_t)slot * E.pages_per_seq + pos / 16];
+                    dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
+                           ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + pos % 16) * 128;
+                }
+            }
+            const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
+                uint32_t lo[16], hi[16];
+                ptx::tmem_ld16(t_head + c * 16, lo);
+                ptx::tmem_ld16(t_head + 64 + c * 16, hi);
+                ptx::tmem_ld_wait();
+                float a[16], b[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    a[j] = has_k ? __uint_as_float(lo[j]) : 0.f;
+                    b[j] = has_k ? __uint_as_float(hi[j]) : 0.f;
+                }
+                if (rotate && dst0) {
+                    const float4 *cs4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)pos * 64 + 16 * c);
+                    const float4 *sn4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)pos * 64 + 16 * c);
+                    const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
+                    const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
+                    float cf[16], sf[16], wl[16], wh[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 cv = cs4[q], sv = sn4[q];
+                        cf[4 * q] = cv.x; cf[4 * q + 1] = cv.y; cf[4 * q + 2] = cv.z; cf[4 * q + 3] = cv.w;
+                        sf[4 * q] = sv.x; sf[4 * q + 1] = sv.y; sf[4 * q + 2] = sv.z; sf[4 * q + 3] = sv.w;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const uint4 l = wl4[q], h = wh4[q];
+                        const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            wl[8 * q + 2 * e] = __uint_as_float(lw[e] << 16);
+                            wl[8 * q + 2 * e + 1] = __uint_as_float(lw[e] & 0xFFFF0000u);
+                            wh[8 * q + 2 * e] = __uint_as_float(hw[e] << 16);
+                            wh[8 * q + 2 * e + 1] = __uint_as_float(hw[e] & 0xFFFF0000u);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float x0 = a[j] * r * wl[j], x1 = b[j] * r * wh[j];
+                        a[j] = x0 * cf[j] - x1 * sf[j];
+                        b[j] = x1 * cf[j] + x0 * sf[j];
+                    }
+                }
+                if (dst0) {
+                    uint32_t pl[8], ph[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        pl[e] = pack_bf16(a[2 * e], a[2 * e + 1]);
+                        ph[e] = pack_bf16(b[2 * e], b[2 * e + 1]);
+                    }
+                    const uint4 l0 = make_uint4(pl[0], pl[1], pl[2], pl[3]), l1 = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+                    const uint4 h0 = make_uint4(ph[0], ph[1], ph[2], ph[3]), h1 = make_uint4(ph[4], ph[5], ph[6], ph[7]);
+                    uint4 *d0 = reinterpret_cast<uint4 *>(dst0 + 16 * c);
+                    uint4 *e0 = reinterpret_cast<uint4 *>(dst0 + 64 + 16 * c);
+                    d0[0] = l0; d0[1] = l1; e0[0] = h0; e0[1] = h1;
+                    if (dst1) {
+                        uint4 *d1 = reinterpret_cast<uint4 *>(dst1 + 16 * c);
+                        uint4 *e1 = reinterpret_cast<uint4 *>(dst1 + 64 + 16 * c);
+                        d1[0] = l0; d1[1] = l1; e1[0] = h0; e1[1] = h1;
+                    }
+                }
+            }
+        }
+    } else if (EPI == EPI_SWIGLU) {
+        for (int b = 0; b < BN / 128; ++b) {
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j) {
+                uint32_t g[16], u[16];
+                ptx::tmem_ld16(t_row + b * 128 + j * 16, g);
+                ptx::tmem_ld16(t_row + b * 128 + 64 + j * 16, u);
+                ptx::tmem_ld_wait();
+                if (row < args.M && n0 + b * 128 < args.N) {
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        float g0 = has_k ? __uint_as_float(g[2 * e]) : 0.f;
+                        float g1 = has_k ? __uint_as_float(g[2 * e + 1]) : 0.f;
+                        float u0 = has_k ? __uint_as_float(u[2 * e]) : 0.f;
+                        float u1 = has_k ? __uint_as_float(u[2 * e + 1]) : 0.f;
+                        packed[e] = pack_bf16(silu_f(g0) * u0, silu_f(g1) * u1);
+                    }
+                    __nv_bfloat16 *dst = args.out_bf16 + (size_t)row * args.ldo + (n0 + b * 128) / 2 + j * 16;
+                    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+                    d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                    d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                }
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 16; ++c) {
+            uint32_t v[16];
+            ptx::tmem_ld16(t_row + c * 16, v);
+            ptx::tmem_ld_wait();
+            if (!has_k)
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = 0;
+            const int col = n0 + c * 16;
+            if (col >= args.N) continue;
+            const int ncols = min(16, args.N - col);
+            if (EPI == EPI_PARTIAL) {
+                if (row < args.M) {
+                    float *p = args.partial + (size_t)split * args.split_stride + (size_t)col * args.ldo + row;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        if (e < ncols) p[(size_t)e * args.ldo] = __uint_as_float(v[e]);
+                }
+            } else if (row < args.M) {
+                if (EPI == EPI_BF16) {
+                    __nv_bfloat16 *dst = args.out_bf16 + (size_t)row * args.ldo + col;
+                    if (ncols == 16) {
+                        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+                        d4[0] = make_uint4(pack_bf16(__uint_as_float(v[0]), __uint_as_float(v[1])),
+                                           pack_bf16(__uint_as_float(v[2]), __uint_as_float(v[3])),
+                                           pack_bf16(__uint_as_float(v[4]), __uint_as_float(v[5])),
+                                           pack_bf16(__uint_as_float(v[6]), __uint_as_float(v[7])));
+                        d4[1] = make_uint4(pack_bf16(__uint_as_float(v[8]), __uint_as_float(v[9])),
+                                           pack_bf16(__uint_as_float(v[10]), __uint_as_float(v[11])),
+                                           pack_bf16(__uint_as_float(v[12]), __uint_as_float(v[13])),
+                                           pack_bf16(__uint_as_float(v[14]), __uint_as_float(v[15])));
+                    } else {
+                        for (int e = 0; e < ncols; ++e) dst[e] = __float2bfloat16_rn(__uint_as_float(v[e]));
+                    }
+                } else {
+                    float *dst = args.out_f32 + (size_t)row * args.ldo + col;
+                    float f[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+                    if (EPI == EPI_RESID) {
+                        const float *r = args.resid + (size_t)row * args.ldr + col;
+                        if (ncols == 16) {
+#pragma unroll
+                            for (int e4 = 0; e4 < 4; ++e4) {
+                                float4 rv = reinterpret_cast<const float4 *>(r)[e4];
+                                f[4 * e4 + 0] += rv.x;
+                                f[4 * e4 + 1] += rv.y;
+                                f[4 * e4 + 2] += rv.z;
+                                f[4 * e4 + 3] += rv.w;
+                            }
+                        } else {
+                            for (int e = 0; e < ncols; ++e) f[e] += r[e];
+                        }
+                    }
+                    if (ncols == 16) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4)
+                            d4[e4] = make_float4(f[4 * e4], f[4 * e4 + 1], f[4 * e4 + 2], f[4 * e4 + 3]);
+                    } else {
+                        for (int e = 0; e < ncols; ++e) dst[e] = f[e];
+                    }
+                }
+            }
+        }
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -222,205 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
             const int n0 = nb * BN;
             const bool has_k = k1 > k0;
-            if (EPI == EPI_QKV) {
-                // Two light passes over TMEM per 128-column head: the sum of squares, then the RoPE pairs (i, i + 64)
-                // sixteen at a time, normalised, rotated, rounded to bf16 and stored; few registers, vector loads.
-                const QkvEpilogue &E = args.qkv;
-                const bool row_ok = row < args.M;
-                const int pos = row_ok ? E.tok_pos[row] : 0;
-                const int slot = row_ok ? E.tok_slot[row] : 0;
-#pragma unroll 1
-                for (int hh = 0; hh < BN / 128; ++hh) {
-                    const uint32_t t_head = t_row + hh * 128;
-                    const int head_row = (n0 + hh * 128) / 128;
-                    const bool is_q = head_row < E.q_heads, is_k = !is_q && head_row < E.q_heads + E.kv_heads;
-                    const bool rotate = is_q || is_k;
-                    float r = 1.f;
-                    if (rotate) {
-                        float ss = 0.f;
-#pragma unroll 1
-                        for (int c = 0; c < 8; c += 2) {
-                            uint32_t u0[16], u1[16];
-                            ptx::tmem_ld16(t_head + c * 16, u0);
-                            ptx::tmem_ld16(t_head + c * 16 + 16, u1);
-                            ptx::tmem_ld_wait();
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                const float a = __uint_as_float(u0[j]), b = __uint_as_float(u1[j]);
-                                ss = fmaf(a, a, ss);
-                                ss = fmaf(b, b, ss);
-                            }
-                        }
-                        r = rsqrtf(ss / 128.0f + E.eps);
-                    }
-                    __nv_bfloat16 *dst0 = nullptr, *dst1 = nullptr;
-                    if (row_ok && n0 + hh * 128 < args.N) {
-                        if (is_q) {
-                            dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
-                        } else {
-                            const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
-                            dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
-                            const int page = E.pages[(size_t)slot * E.pages_per_seq + pos / 16];
-                            dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
-                                   ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + pos % 16) * 128;
-                        }
-                    }
-                    const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
-#pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
-                        uint32_t lo[16], hi[16];
-                        ptx::tmem_ld16(t_head + c * 16, lo);
-                        ptx::tmem_ld16(t_head + 64 + c * 16, hi);
-                        ptx::tmem_ld_wait();
-                        float a[16], b[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            a[j] = has_k ? __uint_as_float(lo[j]) : 0.f;
-                            b[j] = has_k ? __uint_as_float(hi[j]) : 0.f;
-                        }
-                        if (rotate && dst0) {
-                            const float4 *cs4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)pos * 64 + 16 * c);
-                            const float4 *sn4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)pos * 64 + 16 * c);
-                            const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
-                            const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
-                            float cf[16], sf[16], wl[16], wh[16];
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const float4 cv = cs4[q], sv = sn4[q];
-                                cf[4 * q] = cv.x; cf[4 * q + 1] = cv.y; cf[4 * q + 2] = cv.z; cf[4 * q + 3] = cv.w;
-                                sf[4 * q] = sv.x; sf[4 * q + 1] = sv.y; sf[4 * q + 2] = sv.z; sf[4 * q + 3] = sv.w;
-                            }
-#pragma unroll
-                            for (int q = 0; q < 2; ++q) {
-                                const uint4 l = wl4[q], h = wh4[q];
-                                const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    wl[8 * q + 2 * e] = __uint_as_float(lw[e] << 16);
-                                    wl[8 * q + 2 * e + 1] = __uint_as_float(lw[e] & 0xFFFF0000u);
-                                    wh[8 * q + 2 * e] = __uint_as_float(hw[e] << 16);
-                                    wh[8 * q + 2 * e + 1] = __uint_as_float(hw[e] & 0xFFFF0000u);
-                                }
-                            }
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                const float x0 = a[j] * r * wl[j], x1 = b[j] * r * wh[j];
-                                a[j] = x0 * cf[j] - x1 * sf[j];
-                                b[j] = x1 * cf[j] + x0 * sf[j];
-                            }
-                        }
-                        if (dst0) {
-                            uint32_t pl[8], ph[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                pl[e] = pack_bf16(a[2 * e], a[2 * e + 1]);
-                                ph[e] = pack_bf16(b[2 * e], b[2 * e + 1]);
-                            }
-                            const uint4 l0 = make_uint4(pl[0], pl[1], pl[2], pl[3]), l1 = make_uint4(pl[4], pl[5], pl[6], pl[7]);
-                            const uint4 h0 = make_uint4(ph[0], ph[1], ph[2], ph[3]), h1 = make_uint4(ph[4], ph[5], ph[6], ph[7]);
-                            uint4 *d0 = reinterpret_cast<uint4 *>(dst0 + 16 * c);
-                            uint4 *e0 = reinterpret_cast<uint4 *>(dst0 + 64 + 16 * c);
-                            d0[0] = l0; d0[1] = l1; e0[0] = h0; e0[1] = h1;
-                            if (dst1) {
-                                uint4 *d1 = reinterpret_cast<uint4 *>(dst1 + 16 * c);
-                                uint4 *e1 = reinterpret_cast<uint4 *>(dst1 + 64 + 16 * c);
-                                d1[0] = l0; d1[1] = l1; e1[0] = h0; e1[1] = h1;
-                            }
-                        }
-                    }
-                }
-            } else if (EPI == EPI_SWIGLU) {
-                for (int b = 0; b < BN / 128; ++b) {
-#pragma unroll 1
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t g[16], u[16];
-                        ptx::tmem_ld16(t_row + b * 128 + j * 16, g);
-                        ptx::tmem_ld16(t_row + b * 128 + 64 + j * 16, u);
-                        ptx::tmem_ld_wait();
-                        if (row < args.M && n0 + b * 128 < args.N) {
-                            uint32_t packed[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                float g0 = has_k ? __uint_as_float(g[2 * e]) : 0.f;
-                                float g1 = has_k ? __uint_as_float(g[2 * e + 1]) : 0.f;
-                                float u0 = has_k ? __uint_as_float(u[2 * e]) : 0.f;
-                                float u1 = has_k ? __uint_as_float(u[2 * e + 1]) : 0.f;
-                                packed[e] = pack_bf16(silu_f(g0) * u0, silu_f(g1) * u1);
-                            }
-                            __nv_bfloat16 *dst = args.out_bf16 + (size_t)row * args.ldo + (n0 + b * 128) / 2 + j * 16;
-                            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-                            d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                            d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-                        }
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < BN / 16; ++c) {
-                    uint32_t v[16];
-                    ptx::tmem_ld16(t_row + c * 16, v);
-                    ptx::tmem_ld_wait();
-                    if (!has_k)
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) v[e] = 0;
-                    const int col = n0 + c * 16;
-                    if (col >= args.N) continue;
-                    const int ncols = min(16, args.N - col);
-                    if (EPI == EPI_PARTIAL) {
-                        if (row < args.M) {
-                            float *p = args.partial + (size_t)split * args.split_stride + (size_t)col * args.ldo + row;
-#pragma unroll
-                            for (int e = 0; e < 16; ++e)
-                                if (e < ncols) p[(size_t)e * args.ldo] = __uint_as_float(v[e]);
-                        }
-                    } else if (row < args.M) {
-                        if (EPI == EPI_BF16) {
-                            __nv_bfloat16 *dst = args.out_bf16 + (size_t)row * args.ldo + col;
-                            if (ncols == 16) {
-                                uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-                                d4[0] = make_uint4(pack_bf16(__uint_as_float(v[0]), __uint_as_float(v[1])),
-                                                   pack_bf16(__uint_as_float(v[2]), __uint_as_float(v[3])),
-                                                   pack_bf16(__uint_as_float(v[4]), __uint_as_float(v[5])),
-                                                   pack_bf16(__uint_as_float(v[6]), __uint_as_float(v[7])));
-                                d4[1] = make_uint4(pack_bf16(__uint_as_float(v[8]), __uint_as_float(v[9])),
-                                                   pack_bf16(__uint_as_float(v[10]), __uint_as_float(v[11])),
-                                                   pack_bf16(__uint_as_float(v[12]), __uint_as_float(v[13])),
-                                                   pack_bf16(__uint_as_float(v[14]), __uint_as_float(v[15])));
-                            } else {
-                                for (int e = 0; e < ncols; ++e) dst[e] = __float2bfloat16_rn(__uint_as_float(v[e]));
-                            }
-                        } else {
-                            float *dst = args.out_f32 + (size_t)row * args.ldo + col;
-                            float f[16];
-#pragma unroll
-                            for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
-                            if (EPI == EPI_RESID) {
-                                const float *r = args.resid + (size_t)row * args.ldr + col;
-                                if (ncols == 16) {
-#pragma unroll
-                                    for (int e4 = 0; e4 < 4; ++e4) {
-                                        float4 rv = reinterpret_cast<const float4 *>(r)[e4];
-                                        f[4 * e4 + 0] += rv.x;
-                                        f[4 * e4 + 1] += rv.y;
-                                        f[4 * e4 + 2] += rv.z;
-                                        f[4 * e4 + 3] += rv.w;
-                                    }
-                                } else {
-                                    for (int e = 0; e < ncols; ++e) f[e] += r[e];
-                                }
-                            }
-                            if (ncols == 16) {
-                                float4 *d4 = reinterpret_cast<float4 *>(dst);
-#pragma unroll
-                                for (int e4 = 0; e4 < 4; ++e4)
-                                    d4[e4] = make_float4(f[4 * e4], f[4 * e4 + 1], f[4 * e4 + 2], f[4 * e4 + 3]);
-                            } else {
-                                for (int e = 0; e < ncols; ++e) dst[e] = f[e];
-                            }
-                        }
-                    }
-                }
-            }
+            epilogue_tile<BN, EPI>(args, t_row, row, n0, has_k, split);
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&acc_empty[a]);
@@ -430,6 +439,172 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     ptx::tc_fence_after();
     if (warp == 1) ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ---- CTA-pair variant (tcgen05 cta_group::2) ----------------------------------------------------------------------
+//
+// A cluster of two CTAs on neighbouring SMs shares a 256 x 256 output tile: CTA r loads A rows 128 r..128 r + 127
+// and B rows 128 r..128 r + 127 of the tile (32 KiB a stage, so 7 stages fit), and one thread of the even CTA issues
+// M = 256, N = 256 MMAs that read both CTAs' shared memory and write rows 0..127 of the accumulator into the even CTA's
+// TMEM and rows 128..255 into the odd CTA's. Each CTA thus streams half the B traffic of a 128 x 256 tile for the
+// same MMA work. Both CTAs' loads complete on the even CTA's `full` barrier (armed there for both); the MMA commits
+// arrive on `empty` / `acc_full` in both CTAs; both CTAs' epilogue warps release an accumulator on the even CTA's
+// `acc_empty`. Split-K and the transposed partial epilogue are not offered here.
+constexpr int kPairStages = 7;
+constexpr int kPairStageBytes = 2 * 128 * BK * 2;  // A half + B half
+constexpr int kPairSmem = kPairStages * kPairStageBytes + 1024 + 256;
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     GemmArgs args) {
+    constexpr int S = kPairStages, HALF = 128 * BK * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(smem + S * kPairStageBytes);
+    uint64_t *empty = full + S;
+    uint64_t *acc_full = empty + S;
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = ptx::cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int m_tiles = (args.M + 255) / 256, n_tiles = (args.N + 255) / 256;
+    const int nkb = (args.K + BK - 1) / BK;
+    const int total = m_tiles * n_tiles;
+    uint32_t *err = args.err;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            ptx::mbar_init(&acc_full[a], 1);
+            ptx::mbar_init(&acc_empty[a], 8);  // four epilogue warps in each CTA
+        }
+        ptx::mbar_init(mma_done, 1);
+        ptx::fence_barrier_init();
+        ptx::prefetch_tmap(&tmap_a);
+        ptx::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc_pair(tmem_slot, 512);
+        ptx::tmem_relinquish_pair();
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();  // barriers of both CTAs initialised before any remote arrive or load completes on them
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    ptx::griddep_launch();
+
+    // Tile t -> (m block, n block) of 256 x 256; n fastest.
+    if (warp == 0) {
+        if (ptx::elect_one()) {
+            uint32_t it = 0;
+            bool ok = true;
+            int pre = 0;
+            const int row_a = (int)rank * 128, row_b = (int)rank * 128;
+            if (args.independent && pair < total) {
+                const int mb = pair / n_tiles, nb = pair % n_tiles;
+                pre = min(S, nkb);
+                for (int j = 0; j < pre; ++j) {
+                    uint8_t *sa = smem + j * kPairStageBytes;
+                    if (leader) ptx::mbar_arrive_expect_tx(&full[j], 2 * kPairStageBytes);
+                    const uint32_t bar = ptx::mapa(&full[j], 0);
+                    if (args.independent == 1)
+                        ptx::tma_load_2d_pair(sa, &tmap_a, bar, j * BK, mb * 256 + row_a);
+                    else
+                        ptx::tma_load_2d_pair(sa + HALF, &tmap_b, bar, j * BK, nb * 256 + row_b);
+                }
+            }
+            ptx::griddep_wait();
+            for (int t = pair; t < total && ok; t += npairs) {
+                const int mb = t / n_tiles, nb = t % n_tiles;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    uint8_t *sa = smem + s * kPairStageBytes;
+                    uint8_t *sb = sa + HALF;
+                    const uint32_t bar = ptx::mapa(&full[s], 0);
+                    if ((int)it < pre) {
+                        if (args.independent == 1)
+                            ptx::tma_load_2d_pair(sb, &tmap_b, bar, kb * BK, nb * 256 + row_b);
+                        else
+                            ptx::tma_load_2d_pair(sa, &tmap_a, bar, kb * BK, mb * 256 + row_a);
+                        continue;
+                    }
+                    if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, 0x1011)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * kPairStageBytes);
+                    ptx::tma_load_2d_pair(sa, &tmap_a, bar, kb * BK, mb * 256 + row_a);
+                    ptx::tma_load_2d_pair(sb, &tmap_b, bar, kb * BK, nb * 256 + row_b);
+                }
+            }
+            // Both CTAs' loads complete on the even CTA's barriers: it waits for the last stages to land before the
+            // closing cluster barrier, which keeps either CTA from exiting with a copy in flight.
+            if (leader) {
+                uint32_t first = it > (uint32_t)S ? it - S : 0;
+                for (uint32_t j = first; j < it; ++j) ptx::mbar_wait(&full[j % S], (j / S) & 1, err, 0x1012);
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && ptx::elect_one()) {
+            constexpr uint32_t idesc = ptx::idesc_bf16_f32(256, 256);
+            uint32_t it = 0, local = 0;
+            bool ok = true;
+            for (int t = pair; t < total && ok; t += npairs, ++local) {
+                const int a = local & 1;
+                if (!ptx::mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, err, 0x1013)) break;
+                ptx::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + a * 256;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % S;
+                    if (!ptx::mbar_wait(&full[s], (it / S) & 1, err, 0x1014)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t sa = ptx::smem_u32(smem + s * kPairStageBytes), sb = sa + HALF;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        ptx::mma_bf16_pair(d_tmem, ptx::sw128_kmajor_desc(sa + k * UMMA_K * 2),
+                                           ptx::sw128_kmajor_desc(sb + k * UMMA_K * 2), idesc,
+                                           (kb > 0 || k > 0) ? 1u : 0u);
+                    ptx::mma_commit_pair(&empty[s], 0x3);
+                }
+                ptx::mma_commit_pair(&acc_full[a], 0x3);
+            }
+            ptx::mma_commit_pair(mma_done, 0x1);
+            ptx::mbar_wait(mma_done, 0, err, 0x1015);
+        }
+    } else {
+        ptx::griddep_wait();
+        const int q = warp & 3;
+        uint32_t local = 0;
+        const uint32_t rel0 = ptx::mapa(&acc_empty[0], 0), rel1 = ptx::mapa(&acc_empty[1], 0);
+        for (int t = pair; t < total; t += npairs, ++local) {
+            const int mb = t / n_tiles, nb = t % n_tiles;
+            const int a = local & 1;
+            if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
+            ptx::tc_fence_after();
+            const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
+            const uint32_t t_row = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
+            epilogue_tile<256, EPI>(args, t_row, row, nb * 256, nkb > 0, 0);
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(a ? rel1 : rel0);
+        }
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();  // no CTA frees TMEM or exits while its partner's MMAs or arrivals may still reach it
+    ptx::tc_fence_after();
+    if (warp == 1) ptx::tmem_dealloc_pair(tmem_base, 512);
 }
 
 // ---- host side --------------------------------------------------------------------------------------------------
@@ -485,6 +660,24 @@ cudaError_t launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const GemmAr
     return launch_kernel(gemm_kernel<BN, EPI>, dim3(grid), dim3(kThreads), C::SMEM_BYTES, stream, ta, tb, args);
 }
 
+// One cluster of two CTAs per pair of SMs, persistent over the 256 x 256 tiles.
+template <int EPI>
+cudaError_t launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int sms,
+                        cudaStream_t stream) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+        if (e != cudaSuccess) return e;
+        configured[dev & 63] = true;
+    }
+    const int total = ((args.M + 255) / 256) * ((args.N + 255) / 256);
+    const int pairs = total < sms / 2 ? total : sms / 2;
+    return launch_kernel(gemm_pair_kernel<EPI>, dim3(2 * pairs), dim3(kThreads), kPairSmem, stream, ta, tb, args);
+}
+
 template <int BN>
 cudaError_t launch_epi(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int sms,
                        cudaStream_t stream) {
@@ -529,14 +722,34 @@ const char *gemm_check(const GemmArgs &a) {
         if (((uintptr_t)q.q_out | (uintptr_t)q.k_out | (uintptr_t)q.v_out | (uintptr_t)q.pool) & 15)
             return "the q/k/v epilogue outputs must be 16-byte aligned";
     }
+    if (a.cta_pair < 0 || a.cta_pair > 2) return "cta_pair must be 0, 1 or 2";
+    if (a.cta_pair == 2 && (a.bn != 256 || a.splits != 1 || a.epi == EPI_PARTIAL))
+        return "CTA pairs need bn 256, one split and a non-partial epilogue";
     if (!a.err) return "error word missing";
     return nullptr;
 }
 
+bool gemm_uses_pair(const GemmArgs &a) {
+    if (a.cta_pair == 1) return false;
+    if (a.cta_pair == 2) return true;
+    return a.bn == 256 && a.splits == 1 && a.epi != EPI_PARTIAL && a.M >= 1024;
+}
+
 cudaError_t gemm_launch(const GemmArgs &args, int sms, cudaStream_t stream) {
     CUtensorMap ta, tb;
+    const bool pair = gemm_uses_pair(args);
     if (!make_tmap_2d(&ta, args.A, args.M, args.K, BM)) return cudaErrorInvalidValue;
-    if (!make_tmap_2d(&tb, args.B, args.N, args.K, args.bn)) return cudaErrorInvalidValue;
+    if (!make_tmap_2d(&tb, args.B, args.N, args.K, pair ? 128 : args.bn)) return cudaErrorInvalidValue;
+    if (pair) {
+        switch (args.epi) {
+            case EPI_F32: return launch_pair<EPI_F32>(ta, tb, args, sms, stream);
+            case EPI_RESID: return launch_pair<EPI_RESID>(ta, tb, args, sms, stream);
+            case EPI_SWIGLU: return launch_pair<EPI_SWIGLU>(ta, tb, args, sms, stream);
+            case EPI_BF16: return launch_pair<EPI_BF16>(ta, tb, args, sms, stream);
+            case EPI_QKV: return launch_pair<EPI_QKV>(ta, tb, args, sms, stream);
+        }
+        return cudaErrorInvalidValue;
+    }
     switch (args.bn) {
         case 64: return launch_epi<64>(ta, tb, args, sms, stream);
         case 128: return launch_epi<128>(ta, tb, args, sms, stream);

@@ -119,6 +119,7 @@ lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *d) {
     a.resid = (const float *)d->resid;
     a.ldr = d->ldr;
     a.split_stride = d->split_stride;
+    a.cta_pair = d->cta_pair;
     a.err = device_error_word();
     if (!a.err) return LRM_ERR_CUDA;
     if (d->epilogue < 0 || d->epilogue > 4) return op_fail(LRM_ERR_ARGUMENT, "unknown epilogue");

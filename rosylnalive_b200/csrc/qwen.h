@@ -76,8 +76,7 @@ struct PrefillAttnArgs {
     int nseq, max_len, q_heads, kv_heads;
     float scale_log2;
 };
-cudaError_t launch_prefill_attention(const PrefillAttnArgs &a, cudaStream_t st);
-// The same on tcgen05 tensor cores (TMA tiles, TMEM accumulators); total_tokens = rows of q/k/v.
+// Runs on tcgen05 tensor cores (TMA tiles, TMEM accumulators); total_tokens = rows of q/k/v.
 cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_tokens, uint32_t *err, cudaStream_t st);
 
 // rows[r] = argmax of logits[r] ([R][V] fp32): lowest index of the maximum, 0xFFFFFFFF for a row holding a NaN.

@@ -16,7 +16,8 @@ GEMM_F32, GEMM_RESID, GEMM_SWIGLU, GEMM_PARTIAL, GEMM_BF16 = range(5)
 
 class GemmDesc(ctypes.Structure):
     _fields_ = [("m", I32), ("n", I32), ("k", I32), ("a", U64), ("b", U64), ("epilogue", I32), ("bn", I32),
-                ("splits", I32), ("out", U64), ("ldo", I32), ("resid", U64), ("ldr", I32), ("split_stride", U64)]
+                ("splits", I32), ("out", U64), ("ldo", I32), ("resid", U64), ("ldr", I32), ("split_stride", U64),
+                ("cta_pair", I32)]
 
 
 class PrefillAttnDesc(ctypes.Structure):
@@ -62,15 +63,17 @@ def error_word(clear: bool = True) -> int:
     return v.value
 
 
-def gemm(a, b, out, epilogue=GEMM_F32, resid=None, splits=1, bn=0, ldo=None, split_stride=0, stream=None):
-    """out = epilogue(a @ b.T); a bf16 [m, k], b bf16 [n, k] (torch CUDA tensors)."""
+def gemm(a, b, out, epilogue=GEMM_F32, resid=None, splits=1, bn=0, ldo=None, split_stride=0, cta_pair=0,
+         stream=None):
+    """out = epilogue(a @ b.T); a bf16 [m, k], b bf16 [n, k] (torch CUDA tensors). cta_pair: 0 chooses, 1 one CTA
+    per 128-row tile, 2 two-SM clusters sharing 256 x 256 tiles (bn 256)."""
     m, k = a.shape
     n, k2 = b.shape
     assert k == k2
     d = GemmDesc(m, n, k, a.data_ptr(), b.data_ptr(), epilogue, bn, splits, out.data_ptr(),
                  ldo if ldo is not None else (m if epilogue == GEMM_PARTIAL else out.shape[-1]),
                  resid.data_ptr() if resid is not None else 0, resid.shape[-1] if resid is not None else 0,
-                 split_stride)
+                 split_stride, cta_pair)
     N.check(N.lib().lrm_op_gemm_bf16(_stream(stream), ctypes.byref(d)), None, "gemm")
 
 

@@ -94,3 +94,58 @@ def test_gemm_rejects_bad_arguments():
     out = torch.zeros(64, 64, device="cuda")
     with pytest.raises(ValueError):
         ops.gemm(a, b, out)  # k = 100 is not a multiple of 8
+
+
+# Two-SM clusters (cta_pair=2: tcgen05 cta_group::2, 256 x 256 tiles split over a CTA pair), including tiles whose
+# second CTA holds no valid rows (m <= 128 within a tile) and ragged n.
+@pytest.mark.parametrize("m,n,k", [(256, 256, 1024), (300, 520, 512), (130, 256, 64), (4096, 2048, 1024),
+                                   (1000, 1024, 3072), (77, 136, 136)])
+def test_gemm_pair_f32(m, n, k):
+    a, b = bf16((m, k), seed=11), bf16((n, k), 0.05, seed=12)
+    out = torch.full((m, n), float("nan"), device="cuda")
+    ops.gemm(a, b, out, ops.GEMM_F32, bn=256, cta_pair=2)
+    torch.cuda.synchronize()
+    assert rel(out, a.double() @ b.double().T) < 2e-5
+
+
+def test_gemm_pair_matches_single_cta_bitwise():
+    m, n, k = 1536, 1280, 2048
+    a, b = bf16((m, k), seed=13), bf16((n, k), 0.05, seed=14)
+    o1 = torch.zeros(m, n, device="cuda")
+    o2 = torch.zeros(m, n, device="cuda")
+    ops.gemm(a, b, o1, ops.GEMM_F32, bn=256, cta_pair=1)
+    ops.gemm(a, b, o2, ops.GEMM_F32, bn=256, cta_pair=2)
+    torch.cuda.synchronize()
+    assert rel(o2, a.double() @ b.double().T) < 2e-5
+    assert torch.equal(o1, o2)
+
+
+def test_gemm_pair_resid_swiglu_bf16():
+    m, k = 1100, 1024
+    a = bf16((m, k), seed=15)
+    b = bf16((1024, k), 0.02, seed=16)
+    x = torch.randn(m, 1024, device="cuda")
+    ref = x.double() + a.double() @ b.double().T
+    ops.gemm(a, b, x, ops.GEMM_RESID, resid=x, bn=256, cta_pair=2)
+    torch.cuda.synchronize()
+    assert rel(x, ref) < 2e-5
+
+    bg = bf16((768, k), 0.05, seed=17)
+    out = torch.zeros(m, 384, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(a, bg, out, ops.GEMM_SWIGLU, bn=256, cta_pair=2)
+    torch.cuda.synchronize()
+    y = (a.double() @ bg.double().T).view(m, 6, 2, 64)
+    g, u = y[:, :, 0, :], y[:, :, 1, :]
+    assert rel(out, (g * torch.sigmoid(g) * u).reshape(m, 384)) < 1e-2
+
+    ob = torch.zeros(m, 768, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(a, bg, ob, ops.GEMM_BF16, bn=256, cta_pair=2)
+    torch.cuda.synchronize()
+    assert rel(ob, a.double() @ bg.double().T) < 1e-2
+
+
+def test_gemm_pair_rejects_unsupported():
+    a, b = bf16((256, 256)), bf16((256, 256))
+    out = torch.zeros(256, 256, device="cuda")
+    with pytest.raises(ValueError):
+        ops.gemm(a, b, out, ops.GEMM_F32, bn=128, cta_pair=2)

@@ -58,6 +58,28 @@ def test_prefill_logits_match_oracle(mini):
             assert nxt[i] == int(np.argmax(ref))
 
 
+def test_long_prefill_on_cta_pairs_matches_oracle(mini):
+    # 1,200 prompt tokens: the prefill GEMMs (q/k/v with its norm/RoPE/KV epilogue, o_proj and down with the residual,
+    # gate/up with SwiGLU) run on two-SM clusters from 1,024 rows on.
+    cfg, om, _ = mini
+    weights = S.random_weights(cfg, seed=0)
+    cos, sin = R.t_spec(R.torch_inv_freq_bits(cfg.rope_theta, cfg.head_dim), cfg.max_pos)
+    eng = Qw.QwenEngine(cfg, weights, cos, sin, max_seqs=4, max_tokens=2048, max_batch=4)
+    try:
+        lens = (500, 300, 257, 143)
+        prompts = [S.random_prompt(cfg.vocab, n, seed=40 + i, stream=f"l{i}") for i, n in enumerate(lens)]
+        nxt, logits = eng.prefill([0, 1, 2, 3], prompts, want_logits=True)
+        for i, p in enumerate(prompts):
+            ref = O.forward(om, O.Cache.new(om.config, "f32"), 0, p, "f32", logits_rows="last")[0]
+            assert cosine(logits[i], ref) >= 0.9999, i
+            assert np.max(np.abs(logits[i] - ref)) <= 2e-2, i
+            top2 = np.sort(ref)[-2:]
+            if top2[1] - top2[0] > 0.05:
+                assert nxt[i] == int(np.argmax(ref))
+    finally:
+        eng.close()
+
+
 def test_greedy_decode_matches_oracle(mini):
     cfg, om, eng = mini
     prompts = [S.random_prompt(cfg.vocab, n, seed=10 + i, stream=f"g{i}") for i, n in enumerate((16, 40, 5))]
