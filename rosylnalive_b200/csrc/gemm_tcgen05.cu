@@ -58,7 +58,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+// silu(g) = g / (1 + e^-g) with the approximate division (rcp.approx, about 2 ulp in fp32; the result is rounded to
+// bf16 next), the form the decode path's swiglu_reduce uses too.
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // The epilogue of one accumulator row (thread = TMEM lane): row `row` of the output, columns n0..n0+BN-1, read
 // from tensor memory at t_row (the row's lane, the accumulator's first column). has_k is false for an empty k
@@ -88,12 +90,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_r
                     ptx::tmem_ld16(t_head + c * 16, u0);
                     ptx::tmem_ld16(t_head + c * 16 + 16, u1);
                     ptx::tmem_ld_wait();
+                    // columns in order, as the staged (CTA-pair) epilogue sums them
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float a = __uint_as_float(u0[j]), b = __uint_as_float(u1[j]);
-                        ss = fmaf(a, a, ss);
-                        ss = fmaf(b, b, ss);
-                    }
+                    for (int j = 0; j < 16; ++j) ss = fmaf(__uint_as_float(u0[j]), __uint_as_float(u0[j]), ss);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) ss = fmaf(__uint_as_float(u1[j]), __uint_as_float(u1[j]), ss);
                 }
                 r = rsqrtf(ss / 128.0f + E.eps);
             }
@@ -450,9 +451,262 @@ __global__ void __launch_bounds__(kThreads, 1)
 // same MMA work. Both CTAs' loads complete on the even CTA's `full` barrier (armed there for both); the MMA commits
 // arrive on `empty` / `acc_full` in both CTAs; both CTAs' epilogue warps release an accumulator on the even CTA's
 // `acc_empty`. Split-K and the transposed partial epilogue are not offered here.
-constexpr int kPairStages = 7;
+//
+// The epilogue is staged through shared memory: each thread moves its accumulator row from TMEM into a per-warp
+// buffer of 32 rows x 128 bytes (16-byte chunks XOR-swizzled by row, so the warp's row-wise writes and its
+// line-wise reads are free of bank conflicts), then the warp reads the buffer back eight lanes to a 128-byte row
+// segment, so every global load and store covers whole 128-byte lines. A residual is prefetched into L2 for the
+// whole tile before its accumulator is ready.
+constexpr int kPairStages = 6;
 constexpr int kPairStageBytes = 2 * 128 * BK * 2;  // A half + B half
-constexpr int kPairSmem = kPairStages * kPairStageBytes + 1024 + 256;
+constexpr int kStageBuf = 32 * 128;                 // one warp's 32 rows x 128 bytes
+constexpr int kEpiBytes = 4 * 2 * kStageBuf;        // four epilogue warps, two buffers each
+constexpr int kPairSmem = kPairStages * kPairStageBytes + kEpiBytes + 1024 + 256;
+
+__device__ __forceinline__ uint32_t swz(uint32_t buf, int r, int chunk) {
+    return buf + r * 128 + ((chunk ^ (r & 7)) << 4);
+}
+
+// Writes the 8 bf16 of `v` to dst[0..n) (n < 8: the ragged right edge).
+__device__ __forceinline__ void store_bf16_tail(__nv_bfloat16 *dst, uint4 v, int n) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int e = 0; e < n; ++e) {
+        const uint16_t h = (uint16_t)(w[e >> 1] >> ((e & 1) * 16));
+        dst[e] = *reinterpret_cast<const __nv_bfloat16 *>(&h);
+    }
+}
+
+// One warp's share of a 256 x 256 pair tile: output rows row0..row0+31 (TMEM lanes of t_warp), columns n0..n0+255.
+// buf: the warp's two staging buffers (shared::cta addresses).
+template <int EPI>
+__device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t_warp, int row0, int n0,
+                                                uint32_t buf, int lane) {
+    const int sub = lane & 7, rq = lane >> 3;  // read-back: 16-byte chunk, row within each group of four
+    if (EPI == EPI_F32 || EPI == EPI_RESID) {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {  // 32 fp32 columns a pass
+            const uint32_t b = buf + (c & 1) * kStageBuf;
+            uint32_t v[32];
+            ptx::tmem_ld32(t_warp + c * 32, v);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ptx::st_shared_v4(swz(b, lane, j), v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            __syncwarp();
+            const int col = n0 + c * 32 + sub * 4;
+            const int ncols = min(4, args.N - col);
+            float4 res[8];
+            if (EPI == EPI_RESID) {
+#pragma unroll
+                for (int it = 0; it < 8; ++it) {
+                    const int grow = row0 + 4 * it + rq;
+                    res[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (grow < args.M && ncols == 4)
+                        res[it] = *reinterpret_cast<const float4 *>(args.resid + (size_t)grow * args.ldr + col);
+                }
+            }
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int r = 4 * it + rq, grow = row0 + r;
+                const uint4 u = ptx::ld_shared_v4(swz(b, r, sub));
+                float4 f = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                                       __uint_as_float(u.w));
+                if (grow >= args.M || ncols <= 0) continue;
+                float *dst = args.out_f32 + (size_t)grow * args.ldo + col;
+                if (ncols == 4) {
+                    if (EPI == EPI_RESID) {
+                        f.x += res[it].x;
+                        f.y += res[it].y;
+                        f.z += res[it].z;
+                        f.w += res[it].w;
+                    }
+                    *reinterpret_cast<float4 *>(dst) = f;
+                } else {
+                    const float fe[4] = {f.x, f.y, f.z, f.w};
+                    const float *rr = args.resid + (size_t)grow * args.ldr + col;
+                    for (int e = 0; e < ncols; ++e) dst[e] = EPI == EPI_RESID ? fe[e] + rr[e] : fe[e];
+                }
+            }
+        }
+    } else if (EPI == EPI_BF16) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // 64 columns a pass
+            const uint32_t b = buf + (c & 1) * kStageBuf;
+            uint32_t v[32], w[32];
+            ptx::tmem_ld32(t_warp + c * 64, v);
+            ptx::tmem_ld32(t_warp + c * 64 + 32, w);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                ptx::st_shared_v4(swz(b, lane, j), pack_bf16(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
+                                  pack_bf16(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
+                                  pack_bf16(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
+                                  pack_bf16(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                ptx::st_shared_v4(swz(b, lane, 4 + j),
+                                  pack_bf16(__uint_as_float(w[8 * j]), __uint_as_float(w[8 * j + 1])),
+                                  pack_bf16(__uint_as_float(w[8 * j + 2]), __uint_as_float(w[8 * j + 3])),
+                                  pack_bf16(__uint_as_float(w[8 * j + 4]), __uint_as_float(w[8 * j + 5])),
+                                  pack_bf16(__uint_as_float(w[8 * j + 6]), __uint_as_float(w[8 * j + 7])));
+            __syncwarp();
+            const int col = n0 + c * 64 + sub * 8;
+            const int ncols = min(8, args.N - col);
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int r = 4 * it + rq, grow = row0 + r;
+                const uint4 u = ptx::ld_shared_v4(swz(b, r, sub));
+                if (grow >= args.M || ncols <= 0) continue;
+                __nv_bfloat16 *dst = args.out_bf16 + (size_t)grow * args.ldo + col;
+                if (ncols == 8)
+                    *reinterpret_cast<uint4 *>(dst) = u;
+                else
+                    store_bf16_tail(dst, u, ncols);
+            }
+        }
+    } else if (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {  // 128 accumulator columns (64 gate, 64 up) -> 64 outputs a pass
+            const uint32_t b = buf + (c & 1) * kStageBuf;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                uint32_t g[32], u[32];
+                ptx::tmem_ld32(t_warp + c * 128 + h * 32, g);
+                ptx::tmem_ld32(t_warp + c * 128 + 64 + h * 32, u);
+                ptx::tmem_ld_wait();
+                uint32_t p[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float g0 = __uint_as_float(g[2 * e]), g1 = __uint_as_float(g[2 * e + 1]);
+                    p[e] = pack_bf16(silu_f(g0) * __uint_as_float(u[2 * e]), silu_f(g1) * __uint_as_float(u[2 * e + 1]));
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) ptx::st_shared_v4(swz(b, lane, 4 * h + j), p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+            }
+            __syncwarp();
+            const bool live = n0 + c * 128 < args.N;
+            const int col = (n0 + c * 128) / 2 + sub * 8;
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int r = 4 * it + rq, grow = row0 + r;
+                const uint4 v = ptx::ld_shared_v4(swz(b, r, sub));
+                if (live && grow < args.M)
+                    *reinterpret_cast<uint4 *>(args.out_bf16 + (size_t)grow * args.ldo + col) = v;
+            }
+        }
+    } else if (EPI == EPI_QKV) {
+        // Per 128-column head: the sum of squares, then the RoPE pairs (i, i + 64) sixteen at a time, normalised,
+        // rotated and rounded to bf16 into the two staging buffers (dims 0..63, 64..127); the warp then writes each
+        // row's 256 bytes to its contiguous buffer and, for k and v, to the row's page of the KV cache.
+        const QkvEpilogue &E = args.qkv;
+        const int row = row0 + lane;
+        const bool row_ok = row < args.M;
+        const int pos = row_ok ? E.tok_pos[row] : 0;
+        const int slot = row_ok ? E.tok_slot[row] : 0;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+            if (n0 + hh * 128 >= args.N) break;  // warp-uniform
+            const uint32_t t_head = t_warp + hh * 128;
+            const int head_row = (n0 + hh * 128) / 128;
+            const bool is_q = head_row < E.q_heads, is_k = !is_q && head_row < E.q_heads + E.kv_heads;
+            const bool rotate = is_q || is_k;
+            float r = 1.f;
+            if (rotate) {
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t u[32];
+                    ptx::tmem_ld32(t_head + c * 32, u);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(u[j]), __uint_as_float(u[j]), ss);
+                }
+                r = rsqrtf(ss / 128.0f + E.eps);
+            }
+            __nv_bfloat16 *dst0 = nullptr, *dst1 = nullptr;
+            if (row_ok) {
+                if (is_q) {
+                    dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
+                } else {
+                    const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
+                    dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
+                    const int page = E.pages[(size_t)slot * E.pages_per_seq + pos / 16];
+                    dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
+                           ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + pos % 16) * 128;
+                }
+            }
+            const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
+                uint32_t lo[16], hi[16];
+                ptx::tmem_ld16(t_head + c * 16, lo);
+                ptx::tmem_ld16(t_head + 64 + c * 16, hi);
+                ptx::tmem_ld_wait();
+                float a[16], bb[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    a[j] = __uint_as_float(lo[j]);
+                    bb[j] = __uint_as_float(hi[j]);
+                }
+                if (rotate && row_ok) {
+                    const float4 *cs4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)pos * 64 + 16 * c);
+                    const float4 *sn4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)pos * 64 + 16 * c);
+                    const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
+                    const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
+                    float cf[16], sf[16], wl[16], wh[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 cv = cs4[q], sv = sn4[q];
+                        cf[4 * q] = cv.x; cf[4 * q + 1] = cv.y; cf[4 * q + 2] = cv.z; cf[4 * q + 3] = cv.w;
+                        sf[4 * q] = sv.x; sf[4 * q + 1] = sv.y; sf[4 * q + 2] = sv.z; sf[4 * q + 3] = sv.w;
+                    }
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const uint4 l = wl4[q], h = wh4[q];
+                        const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            wl[8 * q + 2 * e] = __uint_as_float(lw[e] << 16);
+                            wl[8 * q + 2 * e + 1] = __uint_as_float(lw[e] & 0xFFFF0000u);
+                            wh[8 * q + 2 * e] = __uint_as_float(hw[e] << 16);
+                            wh[8 * q + 2 * e + 1] = __uint_as_float(hw[e] & 0xFFFF0000u);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float x0 = a[j] * r * wl[j], x1 = bb[j] * r * wh[j];
+                        a[j] = x0 * cf[j] - x1 * sf[j];
+                        bb[j] = x1 * cf[j] + x0 * sf[j];
+                    }
+                }
+                uint32_t pl[8], ph[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    pl[e] = pack_bf16(a[2 * e], a[2 * e + 1]);
+                    ph[e] = pack_bf16(bb[2 * e], bb[2 * e + 1]);
+                }
+                ptx::st_shared_v4(swz(buf, lane, 2 * c), pl[0], pl[1], pl[2], pl[3]);
+                ptx::st_shared_v4(swz(buf, lane, 2 * c + 1), pl[4], pl[5], pl[6], pl[7]);
+                ptx::st_shared_v4(swz(buf + kStageBuf, lane, 2 * c), ph[0], ph[1], ph[2], ph[3]);
+                ptx::st_shared_v4(swz(buf + kStageBuf, lane, 2 * c + 1), ph[4], ph[5], ph[6], ph[7]);
+            }
+            __syncwarp();
+            // Two rows of 256 bytes per pass: lanes 0..15 row 2 it, lanes 16..31 row 2 it + 1.
+            const int ch = lane & 15, seg = ch >> 3;
+#pragma unroll 4
+            for (int it = 0; it < 16; ++it) {
+                const int rr = 2 * it + (lane >> 4);
+                const uint4 v = ptx::ld_shared_v4(swz(buf + seg * kStageBuf, rr, ch & 7));
+                __nv_bfloat16 *d0 = (__nv_bfloat16 *)__shfl_sync(0xffffffffu, (unsigned long long)dst0, rr);
+                __nv_bfloat16 *d1 = (__nv_bfloat16 *)__shfl_sync(0xffffffffu, (unsigned long long)dst1, rr);
+                if (d0) *reinterpret_cast<uint4 *>(d0 + ch * 8) = v;
+                if (d1) *reinterpret_cast<uint4 *>(d1 + ch * 8) = v;
+            }
+            __syncwarp();
+        }
+    }
+}
+
+
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -461,7 +715,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int S = kPairStages, HALF = 128 * BK * 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = (uint64_t *)(smem + S * kPairStageBytes);
+    uint8_t *epi_bufs = smem + S * kPairStageBytes;
+    uint64_t *full = (uint64_t *)(epi_bufs + kEpiBytes);
     uint64_t *empty = full + S;
     uint64_t *acc_full = empty + S;
     uint64_t *acc_empty = acc_full + 2;
@@ -588,14 +843,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         uint32_t local = 0;
         const uint32_t rel0 = ptx::mapa(&acc_empty[0], 0), rel1 = ptx::mapa(&acc_empty[1], 0);
+        const uint32_t buf = ptx::smem_u32(epi_bufs + (warp - 2) * 2 * kStageBuf);
         for (int t = pair; t < total; t += npairs, ++local) {
             const int mb = t / n_tiles, nb = t % n_tiles;
             const int a = local & 1;
+            const int row0 = mb * 256 + (int)rank * 128 + q * 32;
+            if (EPI == EPI_RESID && row0 + lane < args.M) {
+                const uint32_t bytes = (uint32_t)(min(256, args.N - nb * 256) * 4) & ~15u;
+                if (bytes) ptx::prefetch_l2_bulk(args.resid + (size_t)(row0 + lane) * args.ldr + nb * 256, bytes);
+            }
             if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
             ptx::tc_fence_after();
-            const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
-            const uint32_t t_row = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
-            epilogue_tile<256, EPI>(args, t_row, row, nb * 256, nkb > 0, 0);
+            const uint32_t t_warp = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
+            epilogue_staged<EPI>(args, t_warp, row0, nb * 256, buf, lane);
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(a ? rel1 : rel0);

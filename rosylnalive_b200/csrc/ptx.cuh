@@ -239,6 +239,24 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint3
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Brings `bytes` (a multiple of 16, 16-byte aligned) at `gmem` into L2 without waiting.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *gmem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)gmem), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 // ---- CTA pairs (clusters of two; tcgen05 cta_group::2) ----------------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {

@@ -217,7 +217,7 @@ __global__ void swiglu_reduce_kernel(const float *partial, int splits, size_t sp
         g += partial[s * split_stride + base];
         u += partial[s * split_stride + base + 64];
     }
-    act[e] = __float2bfloat16_rn(g / (1.0f + __expf(-g)) * u);
+    act[e] = __float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * u);  // as the prefill GEMM's SwiGLU epilogue
 }
 
 // ---- argmax -------------------------------------------------------------------------------------------------

@@ -144,6 +144,28 @@ def test_gemm_pair_resid_swiglu_bf16():
     assert rel(ob, a.double() @ bg.double().T) < 1e-2
 
 
+@pytest.mark.parametrize("epi", ["resid", "bf16", "swiglu"])
+def test_gemm_pair_epilogues_match_single_cta_bitwise(epi):
+    # The staged (shared-memory) epilogue of CTA pairs computes exactly what the per-row one does; ragged m and n.
+    m, k = 1300, 1024
+    n = 768 if epi == "swiglu" else 1000
+    a, b = bf16((m, k), seed=18), bf16((n, k), 0.05, seed=19)
+    if epi == "resid":
+        x = torch.randn(m, n, device="cuda")
+        o1, o2 = x.clone(), x.clone()
+        ops.gemm(a, b, o1, ops.GEMM_RESID, resid=o1, bn=256, cta_pair=1)
+        ops.gemm(a, b, o2, ops.GEMM_RESID, resid=o2, bn=256, cta_pair=2)
+    else:
+        width = n // 2 if epi == "swiglu" else n
+        kind = ops.GEMM_SWIGLU if epi == "swiglu" else ops.GEMM_BF16
+        o1 = torch.zeros(m, width, device="cuda", dtype=torch.bfloat16)
+        o2 = torch.full((m, width), 7.0, device="cuda", dtype=torch.bfloat16)
+        ops.gemm(a, b, o1, kind, bn=256, cta_pair=1)
+        ops.gemm(a, b, o2, kind, bn=256, cta_pair=2)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+
+
 def test_gemm_pair_rejects_unsupported():
     a, b = bf16((256, 256)), bf16((256, 256))
     out = torch.zeros(256, 256, device="cuda")
