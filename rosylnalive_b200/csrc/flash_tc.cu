@@ -6,9 +6,10 @@
 // place as bf16 and the P V product reads it from tensor memory, so P never goes through shared memory.
 //   warp 0      TMA producer: Q of both slots once, then K and V tiles (3D tensor maps over [tokens][heads][128],
 //               128-byte swizzle, boxes of 64 dims x 128 rows) into a 2-stage ring with separate K and V barriers;
-//   warp 1      tensor-core issuer (one thread), per key tile j: S_s = Q_s K_j^T for both slots, then
-//               O_s += P_s V_j (V read MN-major straight from its [key][dim] tile). S_s of tile j+1 is only issued
-//               once P_s V_j has completed, since it overwrites P_s;
+//   warp 1      tensor-core issuer (one thread): S_s = Q_s K_0^T for both slots, then per key tile j and slot s
+//               O_s += P_s V_j (V read MN-major straight from its [key][dim] tile) followed at once by
+//               S_s = Q_s K_{j+1}^T. The tensor core executes one thread's MMAs in issue order, so S_{j+1}
+//               overwrites P_s only after P_s V_j has read it;
 //   warps 4..11 softmax, one warpgroup per slot, thread = query row (its TMEM lane): the row of S comes into
 //               registers in one go, keys past the row or the sequence are masked (diagonal and tail tiles only),
 //               P = 2^(S * scale * log2 e - m) is written back as bf16 and summed in fp32. The reference maximum m
@@ -81,8 +82,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *kv_empty = v_full + ST;   // ST
     uint64_t *s_full = kv_empty + ST;   // SLOTS
     uint64_t *p_full = s_full + SLOTS;  // SLOTS
-    uint64_t *pv_done = p_full + SLOTS; // SLOTS
-    uint64_t *fin = pv_done + SLOTS;
+    uint64_t *o_done = p_full + SLOTS;  // SLOTS: the last P V of the slot has completed
+    uint64_t *fin = o_done + SLOTS;
     uint32_t *tmem_slot = (uint32_t *)(fin + 1);
     uint32_t *err = p.err;
 
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < SLOTS; ++s) {
             ptx::mbar_init(&s_full[s], 1);
             ptx::mbar_init(&p_full[s], 4);
-            ptx::mbar_init(&pv_done[s], 1);
+            ptx::mbar_init(&o_done[s], 1);
         }
         ptx::mbar_init(fin, 1);
         ptx::fence_barrier_init();
@@ -146,28 +147,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ptx::elect_one()) {
                 constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(128, 128, false);
                 constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(128, 128, true);
-                bool ok = ptx::mbar_wait(q_full, 0, err, 0x3003);
-                for (int j = 0; ok && j < n_kt; ++j) {
-                    const int st = j % ST;
-                    if (!ptx::mbar_wait(&k_full[st], (j / ST) & 1, err, 0x3004)) break;
-                    const uint32_t aK = ptx::smem_u32(sK + st * TILE);
-                    for (int s = 0; s < nslots && ok; ++s) {
-                        // S_s of this tile overwrites P_s of the previous one: P_s V_{j-1} must have completed.
-                        if (j > 0 && !ptx::mbar_wait(&pv_done[s], (j - 1) & 1, err, 0x3005)) {
-                            ok = false;
-                            break;
-                        }
-                        ptx::tc_fence_after();
-                        const uint32_t aQ = ptx::smem_u32(sQ + s * TILE);
+                // S_s = Q_s K_j^T into slot s's S columns, announced on s_full[s].
+                auto issue_qk = [&](int s, int st) {
+                    const uint32_t aQ = ptx::smem_u32(sQ + s * TILE), aK = ptx::smem_u32(sK + st * TILE);
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
-                            ptx::mma_bf16(tmem + 256 * s, ptx::sw128_kmajor_desc(aQ + off),
-                                          ptx::sw128_kmajor_desc(aK + off), idesc_qk, kk > 0 ? 1u : 0u);
-                        }
-                        ptx::mma_commit(&s_full[s]);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
+                        ptx::mma_bf16(tmem + 256 * s, ptx::sw128_kmajor_desc(aQ + off),
+                                      ptx::sw128_kmajor_desc(aK + off), idesc_qk, kk > 0 ? 1u : 0u);
                     }
-                    if (!ok || !ptx::mbar_wait(&v_full[st], (j / ST) & 1, err, 0x3004)) break;
+                    ptx::mma_commit(&s_full[s]);
+                };
+                bool ok = ptx::mbar_wait(q_full, 0, err, 0x3003) && ptx::mbar_wait(&k_full[0], 0, err, 0x3004);
+                if (ok) {
+                    ptx::tc_fence_after();
+                    for (int s = 0; s < nslots; ++s) issue_qk(s, 0);
+                }
+                // Per key tile j and slot s: O_s += P_s V_j, then at once S_s of tile j + 1. The tensor core runs
+                // the MMAs of one thread in issue order, so that S overwrites P_s only after P_s V_j has read it
+                // (the softmax may rescale O_s once S_{j+1} is complete for the same reason).
+                for (int j = 0; ok && j < n_kt; ++j) {
+                    const int st = j % ST, st1 = (j + 1) % ST;
+                    const bool more = j + 1 < n_kt;
+                    if (!ptx::mbar_wait(&v_full[st], (j / ST) & 1, err, 0x3004)) break;
                     const uint32_t aV = ptx::smem_u32(sV + st * TILE);
                     for (int s = 0; s < nslots; ++s) {
                         if (!ptx::mbar_wait(&p_full[s], j & 1, err, 0x3006)) {
@@ -181,9 +183,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ptx::mma_bf16_ts(tmem + 256 * s + 128, tmem + 256 * s + kk * 8, db, idesc_pv,
                                              (j > 0 || kk > 0) ? 1u : 0u);
                         }
-                        ptx::mma_commit(&pv_done[s]);
+                        if (s == nslots - 1) ptx::mma_commit(&kv_empty[st]);  // K_j and V_j are no longer read
+                        if (!more) {
+                            ptx::mma_commit(&o_done[s]);
+                            continue;
+                        }
+                        if (s == 0 && !ptx::mbar_wait(&k_full[st1], ((j + 1) / ST) & 1, err, 0x3005)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        issue_qk(s, st1);
                     }
-                    ptx::mma_commit(&kv_empty[st]);
                 }
                 // No MMA may still be writing TMEM when it is freed (this matters on the error path).
                 ptx::mma_commit(fin);
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&p_full[s]);
             }
-            if (ok && ptx::mbar_wait(&pv_done[s], (n_kt - 1) & 1, err, 0x3008)) {
+            if (ok && ptx::mbar_wait(&o_done[s], 0, err, 0x3008)) {
                 ptx::tc_fence_after();
                 const float inv = 1.f / l;
                 __nv_bfloat16 *dst = p.out + ((size_t)(start + row) * p.q_heads + h0 + s) * kHeadDim;
