@@ -4,15 +4,17 @@
 // q_heads / kv_heads is odd), so every K/V tile is loaded once for both, and walks the 128-key tiles up to the causal
 // limit. Tensor memory (512 columns) holds per slot S (128 x 128 fp32) and O (128 x 128 fp32); P overwrites S in
 // place as bf16 and the P V product reads it from tensor memory, so P never goes through shared memory.
-//   warp 0      TMA producer: Q of both slots once, then K and V tiles (3D tensor maps over [tokens][heads][128],
-//               128-byte swizzle, boxes of 64 dims x 128 rows) into a 2-stage ring with separate K and V barriers;
+//   warp 0      TMA producer: Q of both slots once, then K_0, V_0, K_1, V_1, ... (3D tensor maps over
+//               [tokens][heads][128], 128-byte swizzle, boxes of 64 dims x 128 rows) through a ring of five 32 KiB
+//               stages; K_j is released once both slots' S_j have read it, V_j after both P V_j;
 //   warp 1      tensor-core issuer (one thread): S_s = Q_s K_0^T for both slots, then per key tile j and slot s
 //               O_s += P_s V_j (V read MN-major straight from its [key][dim] tile) followed at once by
 //               S_s = Q_s K_{j+1}^T. The tensor core executes one thread's MMAs in issue order, so S_{j+1}
 //               overwrites P_s only after P_s V_j has read it;
 //   warps 4..11 softmax, one warpgroup per slot, thread = query row (its TMEM lane): the row of S comes into
 //               registers in one go, keys past the row or the sequence are masked (diagonal and tail tiles only),
-//               P = 2^(S * scale * log2 e - m) is written back as bf16 and summed in fp32. The reference maximum m
+//               P = 2^(S * scale * log2 e - m) is written back as bf16 (announced in two parts, so P V starts on
+//               keys 0..95 while 96..127 are stored) and summed in fp32. The reference maximum m
 //               only moves when a tile's maximum exceeds it by more than 8 (a factor 256 in P); then O is rescaled
 //               in tensor memory, which is safe there because S_j completing implies P V_{j-1} has. At the end O / l
 //               is written as bf16.
@@ -31,15 +33,22 @@
 namespace lrm {
 namespace {
 
-constexpr int TQ = 128, TK = 128, ST = 2, SLOTS = 2;
+constexpr int TQ = 128, TK = 128, KV_ST = 5, SLOTS = 2;
 constexpr int SUB = 128 * 64 * 2;  // one [128 rows][64] bf16 swizzled sub-tile
 constexpr int TILE = 2 * SUB;      // [128 rows][128]
-constexpr int SMEM_BYTES = SLOTS * TILE + ST * 2 * TILE + 1024 + 256;
+constexpr int SMEM_BYTES = SLOTS * TILE + KV_ST * TILE + 1024 + 256;
+constexpr int P_SPLIT = 48;  // P is announced in two parts: keys 0..95 (48 packed columns), then 96..127
 constexpr int kThreads = 384;      // warpgroup 0: producer, issuer (two warps idle); warpgroups 1, 2: softmax
 constexpr int kRegsLaunch = 168;    // 65536 / 384, rounded down to the allocation unit of 8
-constexpr int kRegsControl = 56, kRegsSoftmax = 216;
+constexpr int kRegsControl = 56, kRegsSoftmax = 224;
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split exceeds the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+#ifndef LRM_FLASH_EMU_EVERY
+#define LRM_FLASH_EMU_EVERY 0
+#endif
+// On tiles without masking, every kEmuEvery-th pair of keys takes 2^x from a polynomial on the FMA pipe instead of
+// the transcendental unit, which two softmax warpgroups otherwise saturate (0: never).
+constexpr int kEmuEvery = LRM_FLASH_EMU_EVERY;
 
 struct FlashTcParams {
     const int32_t *cu_seqlens;
@@ -52,6 +61,50 @@ struct FlashTcParams {
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// fp32 pairs on the packed FMA pipe (fma / add .rn.f32x2, sm_100): two results per instruction.
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+    asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x for a pair on the FMA pipe, taking load off the transcendental unit: x = r + f with r = rint(x) (adding
+// 1.5 * 2^23 leaves the integer in the low mantissa bits) and f in [-1/2, 1/2]; 2^f is a degree-4 polynomial fitted
+// here for relative error on [-1/2, 1/2] (2.7e-6 at most in fp32 Horner form, against 2^-9 for the bf16 rounding of
+// P that follows); 2^r enters by adding r to the exponent field (1.5 * 2^23 << 23 vanishes mod 2^32). x is clamped
+// at -126 so the exponent field stays non-negative; masked keys (-inf) never take this path.
+constexpr float kE0 = 0.9999992847442627f, kE1 = 0.6931217908859253f, kE2 = 0.240247443318367f,
+                kE3 = 0.05591784045100212f, kE4 = 0.00957008171826601f;
+__device__ __forceinline__ void exp2_poly2(float &y0, float &y1, float x0, float x1) {
+    constexpr float kRound = 12582912.0f;
+    x0 = fmaxf(x0, -126.0f);
+    x1 = fmaxf(x1, -126.0f);
+    float t0, t1, r0, r1, f0, f1, p0, p1;
+    add2(t0, t1, x0, x1, kRound, kRound);
+    add2(r0, r1, t0, t1, -kRound, -kRound);
+    fma2(f0, f1, r0, r1, -1.0f, -1.0f, x0, x1);
+    fma2(p0, p1, kE4, kE4, f0, f1, kE3, kE3);
+    fma2(p0, p1, p0, p1, f0, f1, kE2, kE2);
+    fma2(p0, p1, p0, p1, f0, f1, kE1, kE1);
+    fma2(p0, p1, p0, p1, f0, f1, kE0, kE0);
+    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -72,17 +125,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sQ = smem;                 // SLOTS tiles
-    uint8_t *sK = sQ + SLOTS * TILE;    // ST tiles
-    uint8_t *sV = sK + ST * TILE;       // ST tiles
-    uint64_t *bars = (uint64_t *)(sV + ST * TILE);
+    uint8_t *sQ = smem;                  // SLOTS tiles
+    uint8_t *sKV = sQ + SLOTS * TILE;    // KV_ST tiles: item 2j is K_j, item 2j + 1 is V_j
+    uint64_t *bars = (uint64_t *)(sKV + KV_ST * TILE);
     uint64_t *q_full = bars;
-    uint64_t *k_full = q_full + 1;      // ST
-    uint64_t *v_full = k_full + ST;     // ST
-    uint64_t *kv_empty = v_full + ST;   // ST
-    uint64_t *s_full = kv_empty + ST;   // SLOTS
-    uint64_t *p_full = s_full + SLOTS;  // SLOTS
-    uint64_t *o_done = p_full + SLOTS;  // SLOTS: the last P V of the slot has completed
+    uint64_t *kv_full = q_full + 1;      // KV_ST
+    uint64_t *kv_empty = kv_full + KV_ST; // KV_ST
+    uint64_t *s_full = kv_empty + KV_ST; // SLOTS
+    uint64_t *p_part = s_full + SLOTS;   // SLOTS: P keys 0..95 written
+    uint64_t *p_full = p_part + SLOTS;   // SLOTS: all of P written
+    uint64_t *o_done = p_full + SLOTS;   // SLOTS: the last P V of the slot has completed
     uint64_t *fin = o_done + SLOTS;
     uint32_t *tmem_slot = (uint32_t *)(fin + 1);
     uint32_t *err = p.err;
@@ -90,13 +142,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     if (threadIdx.x == 0) {
         ptx::mbar_init(q_full, 1);
-        for (int s = 0; s < ST; ++s) {
-            ptx::mbar_init(&k_full[s], 1);
-            ptx::mbar_init(&v_full[s], 1);
+        for (int s = 0; s < KV_ST; ++s) {
+            ptx::mbar_init(&kv_full[s], 1);
             ptx::mbar_init(&kv_empty[s], 1);
         }
         for (int s = 0; s < SLOTS; ++s) {
             ptx::mbar_init(&s_full[s], 1);
+            ptx::mbar_init(&p_part[s], 4);
             ptx::mbar_init(&p_full[s], 4);
             ptx::mbar_init(&o_done[s], 1);
         }
@@ -124,32 +176,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ptx::tma_load_3d(sQ + s * TILE, &tq, q_full, 0, h0 + s, start + q0);
                     ptx::tma_load_3d(sQ + s * TILE + SUB, &tq, q_full, 64, h0 + s, start + q0);
                 }
-                int j = 0;
-                for (; j < n_kt; ++j) {
-                    const int s = j % ST;
-                    if (!ptx::mbar_wait(&kv_empty[s], ((j / ST) & 1) ^ 1, err, 0x3001)) break;
-                    const int rows = start + j * TK;
-                    ptx::mbar_arrive_expect_tx(&k_full[s], TILE);
-                    ptx::tma_load_3d(sK + s * TILE, &tk, &k_full[s], 0, kvh, rows);
-                    ptx::tma_load_3d(sK + s * TILE + SUB, &tk, &k_full[s], 64, kvh, rows);
-                    ptx::mbar_arrive_expect_tx(&v_full[s], TILE);
-                    ptx::tma_load_3d(sV + s * TILE, &tv, &v_full[s], 0, kvh, rows);
-                    ptx::tma_load_3d(sV + s * TILE + SUB, &tv, &v_full[s], 64, kvh, rows);
+                const int n_items = 2 * n_kt;
+                int i = 0;
+                for (; i < n_items; ++i) {
+                    const int st = i % KV_ST;
+                    if (!ptx::mbar_wait(&kv_empty[st], ((i / KV_ST) & 1) ^ 1, err, 0x3001)) break;
+                    const CUtensorMap *map = (i & 1) ? &tv : &tk;
+                    const int rows = start + (i >> 1) * TK;
+                    ptx::mbar_arrive_expect_tx(&kv_full[st], TILE);
+                    ptx::tma_load_3d(sKV + st * TILE, map, &kv_full[st], 0, kvh, rows);
+                    ptx::tma_load_3d(sKV + st * TILE + SUB, map, &kv_full[st], 64, kvh, rows);
                 }
                 // Our own copies in flight must land before the CTA exits (this matters on the error path).
                 ptx::mbar_wait(q_full, 0, err, 0x3002);
-                for (int i = j > ST ? j - ST : 0; i < j; ++i) {
-                    ptx::mbar_wait(&k_full[i % ST], (i / ST) & 1, err, 0x3002);
-                    ptx::mbar_wait(&v_full[i % ST], (i / ST) & 1, err, 0x3002);
-                }
+                for (int k = i > KV_ST ? i - KV_ST : 0; k < i; ++k)
+                    ptx::mbar_wait(&kv_full[k % KV_ST], (k / KV_ST) & 1, err, 0x3002);
             }
         } else if (warp == 1) {
             if (ptx::elect_one()) {
                 constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(128, 128, false);
                 constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(128, 128, true);
-                // S_s = Q_s K_j^T into slot s's S columns, announced on s_full[s].
-                auto issue_qk = [&](int s, int st) {
-                    const uint32_t aQ = ptx::smem_u32(sQ + s * TILE), aK = ptx::smem_u32(sK + st * TILE);
+                // Ring item i: stage i % KV_ST, phase (i / KV_ST) & 1.
+                auto wait_item = [&](int i, uint32_t code) {
+                    return ptx::mbar_wait(&kv_full[i % KV_ST], (i / KV_ST) & 1, err, code);
+                };
+                // S_s = Q_s K_j^T into slot s's S columns, announced on s_full[s]; K_j is released after the last
+                // slot's product.
+                auto issue_qk = [&](int s, int j) {
+                    const uint32_t aQ = ptx::smem_u32(sQ + s * TILE), aK = ptx::smem_u32(sKV + ((2 * j) % KV_ST) * TILE);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
@@ -157,43 +211,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       ptx::sw128_kmajor_desc(aK + off), idesc_qk, kk > 0 ? 1u : 0u);
                     }
                     ptx::mma_commit(&s_full[s]);
+                    if (s == nslots - 1) ptx::mma_commit(&kv_empty[(2 * j) % KV_ST]);
                 };
-                bool ok = ptx::mbar_wait(q_full, 0, err, 0x3003) && ptx::mbar_wait(&k_full[0], 0, err, 0x3004);
+                bool ok = ptx::mbar_wait(q_full, 0, err, 0x3003) && wait_item(0, 0x3004);
                 if (ok) {
                     ptx::tc_fence_after();
                     for (int s = 0; s < nslots; ++s) issue_qk(s, 0);
                 }
-                // Per key tile j and slot s: O_s += P_s V_j, then at once S_s of tile j + 1. The tensor core runs
-                // the MMAs of one thread in issue order, so that S overwrites P_s only after P_s V_j has read it
-                // (the softmax may rescale O_s once S_{j+1} is complete for the same reason).
+                // Per key tile j and slot s: O_s += P_s V_j (keys 0..95 as soon as that part of P is written), then
+                // at once S_s of tile j + 1. The tensor core runs the MMAs of one thread in issue order, so S
+                // overwrites P_s only after P_s V_j has read it (the softmax may rescale O_s once S_{j+1} is
+                // complete for the same reason).
                 for (int j = 0; ok && j < n_kt; ++j) {
-                    const int st = j % ST, st1 = (j + 1) % ST;
                     const bool more = j + 1 < n_kt;
-                    if (!ptx::mbar_wait(&v_full[st], (j / ST) & 1, err, 0x3004)) break;
-                    const uint32_t aV = ptx::smem_u32(sV + st * TILE);
+                    if (!wait_item(2 * j + 1, 0x3004)) break;
+                    const int vst = (2 * j + 1) % KV_ST;
+                    const uint32_t aV = ptx::smem_u32(sKV + vst * TILE);
                     for (int s = 0; s < nslots; ++s) {
+                        const uint32_t tO = tmem + 256 * s + 128, tP = tmem + 256 * s;
+                        if (!ptx::mbar_wait(&p_part[s], j & 1, err, 0x3006)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < 6; ++kk)
+                            ptx::mma_bf16_ts(tO, tP + kk * 8, ptx::sw128_mnmajor_desc(aV + kk * 2048, SUB, 1024),
+                                             idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                         if (!ptx::mbar_wait(&p_full[s], j & 1, err, 0x3006)) {
                             ok = false;
                             break;
                         }
                         ptx::tc_fence_after();
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const uint64_t db = ptx::sw128_mnmajor_desc(aV + kk * 2048, SUB, 1024);
-                            ptx::mma_bf16_ts(tmem + 256 * s + 128, tmem + 256 * s + kk * 8, db, idesc_pv,
-                                             (j > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        if (s == nslots - 1) ptx::mma_commit(&kv_empty[st]);  // K_j and V_j are no longer read
+                        for (int kk = 6; kk < 8; ++kk)
+                            ptx::mma_bf16_ts(tO, tP + kk * 8, ptx::sw128_mnmajor_desc(aV + kk * 2048, SUB, 1024),
+                                             idesc_pv, 1u);
+                        if (s == nslots - 1) ptx::mma_commit(&kv_empty[vst]);  // V_j is no longer read
                         if (!more) {
                             ptx::mma_commit(&o_done[s]);
                             continue;
                         }
-                        if (s == 0 && !ptx::mbar_wait(&k_full[st1], ((j + 1) / ST) & 1, err, 0x3005)) {
+                        if (s == 0 && !wait_item(2 * j + 2, 0x3005)) {
                             ok = false;
                             break;
                         }
                         ptx::tc_fence_after();
-                        issue_qk(s, st1);
+                        issue_qk(s, j + 1);
                     }
                 }
                 // No MMA may still be writing TMEM when it is freed (this matters on the error path).
@@ -227,22 +291,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tmem_ld_wait();
                 const int key0 = j * TK;
                 // Masking is needed when some key of the tile lies past the warp's first row or past the sequence.
-                if (key0 + TK - 1 > q0 + q * 32 || key0 + TK > len) {
+                const bool need_mask = key0 + TK - 1 > q0 + q * 32 || key0 + TK > len;
+                if (need_mask) {
                     const int lim = min(row - key0, len - 1 - key0);  // keys 0..lim of the tile are visible
 #pragma unroll
                     for (int e = 0; e < 128; ++e) x[e] = e <= lim ? x[e] : -INFINITY;
                 }
                 float mx[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) mx[e] = fmaxf(x[e], x[e + 8]);
+                for (int u = 0; u < 8; ++u) mx[u] = fmaxf(x[u], x[u + 8]);
 #pragma unroll
-                for (int e = 16; e < 128; e += 8) {
+                for (int e = 16; e < 128; e += 16) {
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], x[e + u]);
+                    for (int u = 0; u < 8; ++u) mx[u] = max3(mx[u], x[e + u], x[e + 8 + u]);
                 }
                 const float tmax =
-                    fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
-                    sc;
+                    fmaxf(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], max3(mx[5], mx[6], mx[7]))) * sc;
                 bool rescale = false;
                 float alpha = 1.f;
                 if (j == 0) {
@@ -266,18 +330,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 const float nm = -m_ref;
-                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                float la = 0.f, lb = 0.f, lc = 0.f, ld = 0.f;
                 uint32_t pk[64];
+                if (need_mask) {
 #pragma unroll
-                for (int e = 0; e < 64; ++e) {
-                    const float a = ptx::ex2(fmaf(x[2 * e], sc, nm));
-                    const float b = ptx::ex2(fmaf(x[2 * e + 1], sc, nm));
-                    ls[e & 3] += a + b;
-                    pk[e] = pack2(a, b);
+                    for (int e = 0; e < 64; ++e) {
+                        float a, b;
+                        fma2(a, b, x[2 * e], x[2 * e + 1], sc, sc, nm, nm);
+                        a = ptx::ex2(a);
+                        b = ptx::ex2(b);
+                        if (e & 1)
+                            add2(lc, ld, lc, ld, a, b);
+                        else
+                            add2(la, lb, la, lb, a, b);
+                        pk[e] = pack2(a, b);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e) {
+                        float a, b;
+                        fma2(a, b, x[2 * e], x[2 * e + 1], sc, sc, nm, nm);
+                        if (kEmuEvery > 0 && e % kEmuEvery == kEmuEvery - 1) {
+                            exp2_poly2(a, b, a, b);
+                            add2(lc, ld, lc, ld, a, b);
+                        } else {
+                            a = ptx::ex2(a);
+                            b = ptx::ex2(b);
+                            add2(la, lb, la, lb, a, b);
+                        }
+                        pk[e] = pack2(a, b);
+                    }
                 }
-                l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                l += (la + lb) + (lc + ld);
                 ptx::tmem_st32(tS, pk);
-                ptx::tmem_st32(tS + 32, pk + 32);
+                ptx::tmem_st16(tS + 32, *reinterpret_cast<const uint32_t(*)[16]>(pk + 32));
+                ptx::tmem_st_wait();
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&p_part[s]);
+                ptx::tmem_st16(tS + P_SPLIT, *reinterpret_cast<const uint32_t(*)[16]>(pk + P_SPLIT));
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
                 __syncwarp();
