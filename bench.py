@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--no-decode", action="store_true", help="only the config-4 prefill part")
     p.add_argument("--prefill-batch", type=int, default=16, help="config-4 prompts per job")
     p.add_argument("--prefill-len", type=int, default=2048, help="config-4 prompt length")
+    p.add_argument("--op-bench", action="store_true",
+                   help="operator benchmarks only (config 2 attention, config 4 GEMM shapes); one JSON line")
     return p.parse_args()
 
 
@@ -392,8 +394,102 @@ def prefill_bench(eng, cfg, dist, pk, stream, timed, batch=16, L=2048):
                          "note": "whole prefill (GEMMs + attention + norms) against the bf16 GEMM peak"}}
 
 
+def op_bench():
+    """Operator benchmarks on cuda:0 through the C ABI (one JSON line; not the headline): BASELINE config 2 (the
+    standalone GQA attention op: batch 8, 16 query / 8 KV heads, head_dim 128, causal prefill of 2048 tokens and
+    decode of one token over 4096 cached ones, bf16 Q/K/V ~ N(0, 1)) and the four prefill GEMM shapes of config 4
+    (M = 32768 tokens) on one CTA per tile, on CTA pairs, and through torch.matmul (cuBLAS) for comparison. Each
+    timing is the median of 20 launches with a 256 MB buffer written between launches (L2 flush)."""
+    import torch
+
+    from rosylnalive_b200 import ops
+
+    ops.set_device(0)
+    torch.cuda.set_device(0)
+    pk, src = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def med_ms(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        return statistics.median(ts)
+
+    res = {"metric": "operator benchmarks (BASELINE config 2 attention, config 4 GEMM shapes)", "impl": "ours",
+           "peaks": {**pk, "source": src}}
+    # config 2, prefill: packed sequences of 2048 tokens
+    B, L, QH, KVH = 8, 2048, 16, 8
+    T = B * L
+    q = torch.randn(T, QH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(T, KVH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(T, KVH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(T, QH, 128, device="cuda", dtype=torch.bfloat16)
+    cu = torch.arange(0, T + 1, L, device="cuda", dtype=torch.int32)
+    ms = med_ms(lambda: ops.prefill_attention(q, k, v, out, cu, L, 1.0 / 128 ** 0.5))
+    flops = 4.0 * 128 * QH * B * L * (L + 1) / 2
+    res["attention_prefill"] = {"shape": "8 x 2048, 16/8 heads, causal", "ms": ms,
+                                "tflops": flops / ms / 1e9, "frac_of_bf16_peak": flops / ms / 1e9 / pk["bf16_tflops"],
+                                "flops": flops, "note": "causal FLOPs 4*d*heads*sum(L(L+1)/2)"}
+    # config 2, decode: one query per sequence over 4096 cached tokens in 16-token pages
+    C = 4096
+    pages = C // 16
+    pool = torch.randn(B * pages, KVH, 2, 16, 128, device="cuda", generator=g).to(torch.bfloat16)
+    table = torch.randperm(B * pages, device="cuda", generator=g).to(torch.int32).view(B, pages)
+    lens = torch.full((B,), C, dtype=torch.int32, device="cuda")
+    slots = torch.arange(B, dtype=torch.int32, device="cuda")
+    dq = torch.randn(B, QH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    dout = torch.empty(B, QH, 128, device="cuda", dtype=torch.bfloat16)
+    want_ctas = 4 * 148
+    pps = max(1, -(-pages // max(1, -(-want_ctas // (B * KVH)))))
+    ws = torch.empty(ops.decode_attention_workspace(B, KVH, pages, pps) // 4, device="cuda")
+    ms = med_ms(lambda: ops.decode_attention(dq, pool, table, lens, slots, dout, ws, pps, 1.0 / 128 ** 0.5))
+    nbytes = B * C * KVH * 2 * 128 * 2 + dq.numel() * 2 + dout.numel() * 2
+    res["attention_decode"] = {"shape": "8 x 1 query over 4096 cached tokens, 16/8 heads", "ms": ms,
+                               "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / pk["hbm_gbs"],
+                               "bytes": nbytes, "pages_per_split": pps}
+    # config 4 prefill GEMM shapes
+    M = 32768
+    shapes = [("q/k/v", 4096, 1024, ops.GEMM_BF16), ("o_proj + residual", 1024, 2048, ops.GEMM_RESID),
+              ("gate/up + SwiGLU", 6144, 1024, ops.GEMM_SWIGLU), ("down + residual", 1024, 3072, ops.GEMM_RESID)]
+    rows = []
+    for name, n, kk, epi in shapes:
+        a = torch.randn(M, kk, device="cuda", generator=g).to(torch.bfloat16)
+        b = (torch.randn(n, kk, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        if epi == ops.GEMM_SWIGLU:
+            o = torch.empty(M, n // 2, device="cuda", dtype=torch.bfloat16)
+        elif epi == ops.GEMM_BF16:
+            o = torch.empty(M, n, device="cuda", dtype=torch.bfloat16)
+        else:
+            o = torch.zeros(M, n, device="cuda")
+        r = o if epi == ops.GEMM_RESID else None
+        fl = 2.0 * M * n * kk
+        row = {"gemm": name, "m": M, "n": n, "k": kk}
+        for label, pair in (("one_cta", 1), ("cta_pair", 2)):
+            ms = med_ms(lambda: ops.gemm(a, b, o, epi, resid=r, bn=256, cta_pair=pair))
+            row[label + "_tflops"] = fl / ms / 1e9
+        ms = med_ms(lambda: torch.matmul(a, b.T))
+        row["torch_matmul_bf16_out_tflops"] = fl / ms / 1e9
+        row["cta_pair_frac_of_bf16_peak"] = row["cta_pair_tflops"] / pk["bf16_tflops"]
+        rows.append(row)
+    res["gemm_config4"] = rows
+    print(json.dumps(res), flush=True)
+
+
 def main():
     args = parse()
+    if args.op_bench:
+        op_bench()
+        return
     dist = Dist()
     if args.impl == "reference":
         run_reference(args, dist)
