@@ -247,7 +247,8 @@ def run_ours(args, dist):
         eng.close()
         if dist.rank == 0:
             print(json.dumps({"metric": METRIC, "value": prefill["value"], "unit": "tok/s", "n_gpus": dist.world,
-                              "steps": 3, "warmup": 2, "ms_per_step": prefill["ms_per_prefill"],
+                              "steps": prefill["timed_prefills"], "warmup": 2,
+                              "ms_per_step": prefill["ms_per_prefill"],
                               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                               "data": "synthetic", "config": {"workload": prefill["workload"],
                                                               "layers": cfg.layers},
@@ -374,8 +375,18 @@ def prefill_bench(eng, cfg, dist, pk, stream, timed, batch=16, L=2048):
     slots = np.arange(nseq, dtype=np.int32)
     for _ in range(2):
         eng.prefill(slots, prompts)
-    reps = 3
-    ms = timed(lambda: [eng.prefill(slots, prompts) for _ in range(reps)]) / reps
+    # the median of individually timed prefills (max over ranks each), steadier than one short window; clocks are
+    # sampled meanwhile on rank 0
+    import torch
+
+    sampler = None
+    if dist.rank == 0:
+        u = str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+        sampler = ClockSampler([u if u.startswith("GPU-") else f"GPU-{u}"])
+        sampler.start()
+    samples = [timed(lambda: eng.prefill(slots, prompts)) for _ in range(8)]
+    clocks = sampler.stop() if sampler else None
+    ms = statistics.median(samples)
     tokens_job = nseq * dist.world * L
     # algorithmic FLOPs per GPU (the reference's OpCost conventions): GEMMs 2 * params * tokens, attention
     # 4 * hd * (causal pairs) per head and layer, lm_head on the last rows
@@ -388,6 +399,7 @@ def prefill_bench(eng, cfg, dist, pk, stream, timed, batch=16, L=2048):
     flops = gemm_flops + attn_flops + head_flops
     achieved = flops / (ms / 1000.0) / 1e12
     return {"value": tokens_job / (ms / 1000.0), "unit": "tok/s", "ms_per_prefill": ms,
+            "ms_min_max": [min(samples), max(samples)], "timed_prefills": len(samples), "clocks": clocks,
             "workload": f"config4: {nseq * dist.world} x {L}-token prompts, {nseq} per GPU (strong scaling)",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": achieved / pk["bf16_tflops"], "flops_per_gpu": flops,

@@ -593,120 +593,131 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
                     *reinterpret_cast<uint4 *>(args.out_bf16 + (size_t)grow * args.ldo + col) = v;
             }
         }
-    } else if (EPI == EPI_QKV) {
-        // Per 128-column head: the sum of squares, then the RoPE pairs (i, i + 64) sixteen at a time, normalised,
-        // rotated and rounded to bf16 into the two staging buffers (dims 0..63, 64..127); the warp then writes each
-        // row's 256 bytes to its contiguous buffer and, for k and v, to the row's page of the KV cache.
-        const QkvEpilogue &E = args.qkv;
-        const int row = row0 + lane;
-        const bool row_ok = row < args.M;
-        const int pos = row_ok ? E.tok_pos[row] : 0;
-        const int slot = row_ok ? E.tok_slot[row] : 0;
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-            if (n0 + hh * 128 >= args.N) break;  // warp-uniform
-            const uint32_t t_head = t_warp + hh * 128;
-            const int head_row = (n0 + hh * 128) / 128;
-            const bool is_q = head_row < E.q_heads, is_k = !is_q && head_row < E.q_heads + E.kv_heads;
-            const bool rotate = is_q || is_k;
-            float r = 1.f;
-            if (rotate) {
-                float ss = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t u[32];
-                    ptx::tmem_ld32(t_head + c * 32, u);
-                    ptx::tmem_ld_wait();
+    }
+}
+
+// The row's RoPE table entries (cos and sin of its position), loaded before the accumulator is ready: they depend
+// only on the token, so their latency hides behind the main loop and both heads of the tile use them.
+struct QkvRow {
+    float cs[64], sn[64];
+    int pos, slot;
+    bool ok;
+};
+
+__device__ __forceinline__ void qkv_preload(const GemmArgs &args, int row, bool rotates, QkvRow &R) {
+    const QkvEpilogue &E = args.qkv;
+    R.ok = row < args.M;
+    R.pos = R.ok ? E.tok_pos[row] : 0;
+    R.slot = R.ok ? E.tok_slot[row] : 0;
+    if (rotates && R.ok) {
+        const float4 *c4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)R.pos * 64);
+        const float4 *s4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)R.pos * 64);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(u[j]), __uint_as_float(u[j]), ss);
-                }
-                r = rsqrtf(ss / 128.0f + E.eps);
-            }
-            __nv_bfloat16 *dst0 = nullptr, *dst1 = nullptr;
-            if (row_ok) {
-                if (is_q) {
-                    dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
-                } else {
-                    const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
-                    dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
-                    const int page = E.pages[(size_t)slot * E.pages_per_seq + pos / 16];
-                    dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
-                           ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + pos % 16) * 128;
-                }
-            }
-            const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
-                uint32_t lo[16], hi[16];
-                ptx::tmem_ld16(t_head + c * 16, lo);
-                ptx::tmem_ld16(t_head + 64 + c * 16, hi);
-                ptx::tmem_ld_wait();
-                float a[16], bb[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    a[j] = __uint_as_float(lo[j]);
-                    bb[j] = __uint_as_float(hi[j]);
-                }
-                if (rotate && row_ok) {
-                    const float4 *cs4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)pos * 64 + 16 * c);
-                    const float4 *sn4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)pos * 64 + 16 * c);
-                    const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
-                    const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
-                    float cf[16], sf[16], wl[16], wh[16];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 cv = cs4[q], sv = sn4[q];
-                        cf[4 * q] = cv.x; cf[4 * q + 1] = cv.y; cf[4 * q + 2] = cv.z; cf[4 * q + 3] = cv.w;
-                        sf[4 * q] = sv.x; sf[4 * q + 1] = sv.y; sf[4 * q + 2] = sv.z; sf[4 * q + 3] = sv.w;
-                    }
-#pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const uint4 l = wl4[q], h = wh4[q];
-                        const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            wl[8 * q + 2 * e] = __uint_as_float(lw[e] << 16);
-                            wl[8 * q + 2 * e + 1] = __uint_as_float(lw[e] & 0xFFFF0000u);
-                            wh[8 * q + 2 * e] = __uint_as_float(hw[e] << 16);
-                            wh[8 * q + 2 * e + 1] = __uint_as_float(hw[e] & 0xFFFF0000u);
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float x0 = a[j] * r * wl[j], x1 = bb[j] * r * wh[j];
-                        a[j] = x0 * cf[j] - x1 * sf[j];
-                        bb[j] = x1 * cf[j] + x0 * sf[j];
-                    }
-                }
-                uint32_t pl[8], ph[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    pl[e] = pack_bf16(a[2 * e], a[2 * e + 1]);
-                    ph[e] = pack_bf16(bb[2 * e], bb[2 * e + 1]);
-                }
-                ptx::st_shared_v4(swz(buf, lane, 2 * c), pl[0], pl[1], pl[2], pl[3]);
-                ptx::st_shared_v4(swz(buf, lane, 2 * c + 1), pl[4], pl[5], pl[6], pl[7]);
-                ptx::st_shared_v4(swz(buf + kStageBuf, lane, 2 * c), ph[0], ph[1], ph[2], ph[3]);
-                ptx::st_shared_v4(swz(buf + kStageBuf, lane, 2 * c + 1), ph[4], ph[5], ph[6], ph[7]);
-            }
-            __syncwarp();
-            // Two rows of 256 bytes per pass: lanes 0..15 row 2 it, lanes 16..31 row 2 it + 1.
-            const int ch = lane & 15, seg = ch >> 3;
-#pragma unroll 4
-            for (int it = 0; it < 16; ++it) {
-                const int rr = 2 * it + (lane >> 4);
-                const uint4 v = ptx::ld_shared_v4(swz(buf + seg * kStageBuf, rr, ch & 7));
-                __nv_bfloat16 *d0 = (__nv_bfloat16 *)__shfl_sync(0xffffffffu, (unsigned long long)dst0, rr);
-                __nv_bfloat16 *d1 = (__nv_bfloat16 *)__shfl_sync(0xffffffffu, (unsigned long long)dst1, rr);
-                if (d0) *reinterpret_cast<uint4 *>(d0 + ch * 8) = v;
-                if (d1) *reinterpret_cast<uint4 *>(d1 + ch * 8) = v;
-            }
-            __syncwarp();
+        for (int i = 0; i < 16; ++i) {
+            const float4 c = c4[i], sv = s4[i];
+            R.cs[4 * i] = c.x; R.cs[4 * i + 1] = c.y; R.cs[4 * i + 2] = c.z; R.cs[4 * i + 3] = c.w;
+            R.sn[4 * i] = sv.x; R.sn[4 * i + 1] = sv.y; R.sn[4 * i + 2] = sv.z; R.sn[4 * i + 3] = sv.w;
         }
     }
 }
 
-
+// EPI_QKV for one warp's 32 rows of a pair tile (two 128-column heads): per head the sum of squares, then the RoPE
+// pairs (i, i + 64) sixteen at a time, normalised, rotated and rounded to bf16 into the two staging buffers (dims
+// 0..63, 64..127); the warp then writes each row's 256 bytes to its contiguous buffer and, for k and v, to the row's
+// page of the KV cache.
+__device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32_t t_warp, int n0, uint32_t buf,
+                                                    int lane, int row, const QkvRow &R) {
+    const QkvEpilogue &E = args.qkv;
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+        if (n0 + hh * 128 >= args.N) break;  // warp-uniform
+        const uint32_t t_head = t_warp + hh * 128;
+        const int head_row = (n0 + hh * 128) / 128;
+        const bool is_q = head_row < E.q_heads, is_k = !is_q && head_row < E.q_heads + E.kv_heads;
+        const bool rotate = is_q || is_k;
+        float r = 1.f;
+        if (rotate) {
+            float ss = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t u[32];
+                ptx::tmem_ld32(t_head + c * 32, u);
+                ptx::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(u[j]), __uint_as_float(u[j]), ss);
+            }
+            r = rsqrtf(ss / 128.0f + E.eps);
+        }
+        __nv_bfloat16 *dst0 = nullptr, *dst1 = nullptr;
+        if (R.ok) {
+            if (is_q) {
+                dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
+            } else {
+                const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
+                dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
+                const int page = E.pages[(size_t)R.slot * E.pages_per_seq + R.pos / 16];
+                dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
+                       ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + R.pos % 16) * 128;
+            }
+        }
+        const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
+            uint32_t lo[16], hi[16];
+            ptx::tmem_ld16(t_head + c * 16, lo);
+            ptx::tmem_ld16(t_head + 64 + c * 16, hi);
+            ptx::tmem_ld_wait();
+            float a[16], bb[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                a[j] = __uint_as_float(lo[j]);
+                bb[j] = __uint_as_float(hi[j]);
+            }
+            if (rotate && R.ok) {
+                const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
+                const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const uint4 l = wl4[q], h = wh4[q];
+                    const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int j = 8 * q + e;
+                        const float wl = __uint_as_float((e & 1) ? (lw[e >> 1] & 0xFFFF0000u) : (lw[e >> 1] << 16));
+                        const float wh = __uint_as_float((e & 1) ? (hw[e >> 1] & 0xFFFF0000u) : (hw[e >> 1] << 16));
+                        const float x0 = a[j] * r * wl, x1 = bb[j] * r * wh;
+                        const float cf = R.cs[16 * c + j], sf = R.sn[16 * c + j];
+                        a[j] = x0 * cf - x1 * sf;
+                        bb[j] = x1 * cf + x0 * sf;
+                    }
+                }
+            }
+            uint32_t pl[8], ph[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                pl[e] = pack_bf16(a[2 * e], a[2 * e + 1]);
+                ph[e] = pack_bf16(bb[2 * e], bb[2 * e + 1]);
+            }
+            ptx::st_shared_v4(swz(buf, lane, 2 * c), pl[0], pl[1], pl[2], pl[3]);
+            ptx::st_shared_v4(swz(buf, lane, 2 * c + 1), pl[4], pl[5], pl[6], pl[7]);
+            ptx::st_shared_v4(swz(buf + kStageBuf, lane, 2 * c), ph[0], ph[1], ph[2], ph[3]);
+            ptx::st_shared_v4(swz(buf + kStageBuf, lane, 2 * c + 1), ph[4], ph[5], ph[6], ph[7]);
+        }
+        __syncwarp();
+        // Two rows of 256 bytes per pass: lanes 0..15 row 2 it, lanes 16..31 row 2 it + 1.
+        const int ch = lane & 15, seg = ch >> 3;
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+            const int rr = 2 * it + (lane >> 4);
+            const uint4 v = ptx::ld_shared_v4(swz(buf + seg * kStageBuf, rr, ch & 7));
+            __nv_bfloat16 *d0 = (__nv_bfloat16 *)__shfl_sync(0xffffffffu, (unsigned long long)dst0, rr);
+            __nv_bfloat16 *d1 = (__nv_bfloat16 *)__shfl_sync(0xffffffffu, (unsigned long long)dst1, rr);
+            if (d0) *reinterpret_cast<uint4 *>(d0 + ch * 8) = v;
+            if (d1) *reinterpret_cast<uint4 *>(d1 + ch * 8) = v;
+        }
+        __syncwarp();
+    }
+}
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -852,10 +863,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t bytes = (uint32_t)(min(256, args.N - nb * 256) * 4) & ~15u;
                 if (bytes) ptx::prefetch_l2_bulk(args.resid + (size_t)(row0 + lane) * args.ldr + nb * 256, bytes);
             }
-            if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
-            ptx::tc_fence_after();
-            const uint32_t t_warp = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
-            epilogue_staged<EPI>(args, t_warp, row0, nb * 256, buf, lane);
+            if constexpr (EPI == EPI_QKV) {
+                QkvRow R;
+                qkv_preload(args, row0 + lane, nb * 256 < (args.qkv.q_heads + args.qkv.kv_heads) * 128, R);
+                if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
+                ptx::tc_fence_after();
+                const uint32_t t_warp = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
+                epilogue_qkv_staged(args, t_warp, nb * 256, buf, lane, row0 + lane, R);
+            } else {
+                if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
+                ptx::tc_fence_after();
+                const uint32_t t_warp = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
+                epilogue_staged<EPI>(args, t_warp, row0, nb * 256, buf, lane);
+            }
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(a ? rel1 : rel0);
