@@ -308,6 +308,10 @@ __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, in
 // combine kernel merges the splits.
 template <int ST>
 __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
+    // Consumer warp w takes the pages j = w (mod 4) and page j sits in stage j % ST. With ST a multiple of 4 every
+    // stage belongs to one warp, which waits on it phase after phase. Otherwise a warp running ahead could wait on a
+    // phase two beyond the barrier's current one, which the parity test cannot tell from a completed phase.
+    static_assert(ST % 4 == 0, "the stage count must be a multiple of the four consumer warps");
     constexpr int PAGE_BYTES = 2 * kPageTokens * kHeadDim * 2;  // K + V of one head = 8 KiB
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *stages = smem_raw;
@@ -549,7 +553,7 @@ cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_
 }
 
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
-    constexpr int ST = 8;
+    constexpr int ST = 4;  // 37 KiB of shared memory a CTA, five CTAs an SM (measured faster than 8 / 12 / 16)
     const size_t smem = ST * 8192 + (4 * 32 + 4 * 2 * 128 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
     static bool configured[64] = {};
     int dev = 0;
