@@ -34,7 +34,8 @@ typedef enum lrm_status {
     LRM_ERR_ARGUMENT = 4,      /* a null handle/pointer or an impossible size */
     LRM_ERR_OUT_OF_MEMORY = 5, /* device memory allocation failed */
     LRM_ERR_STATE = 6,         /* call out of order: heap/table twice, list reused, ... */
-    LRM_ERR_NO_DEVICE = 7      /* no CUDA device with that index */
+    LRM_ERR_NO_DEVICE = 7,     /* no CUDA device with that index */
+    LRM_ERR_FORMAT = 8         /* a file breaks its format (SafetensorsFormatException, Safetensors.fs:16) */
 } lrm_status;
 
 typedef struct lrm_device_s *lrm_device;   /* IGpuBackend (+ its IGpuHeap, created once) */
@@ -311,6 +312,49 @@ lrm_status lrm_qwen_stream(lrm_qwen q, void **stream);
 
 /* Current length of a slot. */
 lrm_status lrm_qwen_seq_len(lrm_qwen q, int32_t slot, int32_t *len);
+
+/* Loads every tensor of a safetensors checkpoint (HF names, as lrm_qwen_set_weight takes them) into the engine,
+ * streaming it from the memory-mapped file through two pinned 64 MiB buffers on the engine's stream. BF16 tensors are
+ * copied as they are; F32 tensors are narrowed to bf16 (round to nearest even). A name that is not a weight of this
+ * model, another dtype or a wrong element count is refused (LRM_ERR_ARGUMENT) before anything of that tensor is
+ * copied; a malformed file gives LRM_ERR_FORMAT. `loaded` (may be null) receives the number of tensors loaded.
+ * Replaces the reference's streamed SafetensorsFile reads with 64 MiB UploadFrom (Safetensors.fs:504-727,
+ * docs/contracts/gpu-backend.md:56). */
+lrm_status lrm_qwen_load_safetensors(lrm_qwen q, const char *path, int32_t *loaded);
+
+/* ---- safetensors reader (SafetensorsFile, src/Lrm.Tensor/Safetensors.fs:231-727) --------------------------------
+ * Open maps the file read-only and validates the whole header before anything is returned: the 8-byte length
+ * (<= 100,000,000 and within the file), strict UTF-8 and JSON (depth <= 8, \u escapes forming valid Unicode), no
+ * duplicate key, __metadata__ an object of strings, every tensor with exactly dtype / shape / data_offsets, its byte
+ * count equal to the shape's, and the tensors tiling the data section exactly. Failures are LRM_ERR_FORMAT with a
+ * message naming the file (lrm_cuda_last_error(NULL, ...)). Entries and metadata come in code point order of their
+ * names. Pointers returned (names, shapes, data) stay valid until lrm_st_close. Needs no GPU. */
+typedef struct lrm_st_file_s *lrm_st_file;
+typedef enum lrm_st_dtype {
+    LRM_ST_F32 = 0, LRM_ST_F64 = 1, LRM_ST_BF16 = 2, LRM_ST_F16 = 3,
+    LRM_ST_I32 = 4, LRM_ST_U32 = 5, LRM_ST_U8 = 6, LRM_ST_I64 = 7
+} lrm_st_dtype;
+typedef struct lrm_st_entry {
+    const char *name;     /* UTF-8 */
+    int32_t dtype;        /* lrm_st_dtype */
+    int32_t rank;
+    const int64_t *shape; /* [rank] */
+    uint64_t begin, end;  /* byte offsets within the data section */
+    const void *data;     /* the tensor's bytes in the mapped file */
+} lrm_st_entry;
+
+lrm_status lrm_st_open(const char *path, lrm_st_file *out);
+lrm_status lrm_st_close(lrm_st_file f);
+/* Validates a file image in memory (SafetensorsFile.Validate): header length and tensor count on success. */
+lrm_status lrm_st_validate(const void *bytes, uint64_t length, uint64_t *header_len, int64_t *count);
+/* File length, header length N (the data section starts at 8 + N), tensor and metadata counts, and whether the data
+ * section starts at a multiple of 8 with every tensor at a multiple of its element size (IsAligned). */
+lrm_status lrm_st_info(lrm_st_file f, uint64_t *length, uint64_t *header_len, int64_t *count, int64_t *metadata_count,
+                       int32_t *aligned);
+lrm_status lrm_st_entry_at(lrm_st_file f, int64_t index, lrm_st_entry *out);
+/* LRM_ERR_ARGUMENT when the file has no tensor of that name. */
+lrm_status lrm_st_find(lrm_st_file f, const char *name, lrm_st_entry *out);
+lrm_status lrm_st_metadata_at(lrm_st_file f, int64_t index, const char **key, const char **value);
 
 /* ---- host helpers ------------------------------------------------------------------------------------------- */
 

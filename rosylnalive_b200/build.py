@@ -31,6 +31,7 @@ SOURCES = [
     "flash_tc.cu",
     "qwen_engine.cu",
     "decode_attn_static.cu",
+    "safetensors.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -396,44 +396,158 @@ lrm_status lrm_qwen_destroy(lrm_qwen Q) {
     return LRM_OK;
 }
 
+// Where an HF-named weight lives on the device: `count` bf16 elements at `dst`, or for gate/up (interleave 0 / 64)
+// rows j at row (j / 64) * 128 + interleave + j % 64 of w_gu (64-row blocks, so a 128-column GEMM tile holds matching
+// gate and up columns).
+struct WeightDst {
+    __nv_bfloat16 *dst = nullptr;
+    uint64_t count = 0;
+    int interleave = -1;
+};
+
+static lrm_status resolve_weight(lrm_qwen Q, const std::string &n, WeightDst &w) {
+    const lrm_qwen_config &c = Q->c;
+    const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
+    auto set = [&](__nv_bfloat16 *d, uint64_t cnt, int il = -1) {
+        w.dst = d;
+        w.count = cnt;
+        w.interleave = il;
+        return LRM_OK;
+    };
+    if (n == "model.embed_tokens.weight") return set(Q->embed, (uint64_t)c.vocab * H);
+    if (n == "model.norm.weight") return set(Q->final_norm, H);
+    int layer = -1, consumed = 0;
+    if (sscanf(n.c_str(), "model.layers.%d.%n", &layer, &consumed) != 1 || consumed == 0 || layer < 0 ||
+        layer >= c.layers)
+        return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name of this model");
+    Layer &L = Q->layers[layer];
+    const std::string rest = n.substr(consumed);
+    if (rest == "input_layernorm.weight") return set(L.in_norm, H);
+    if (rest == "post_attention_layernorm.weight") return set(L.post_norm, H);
+    if (rest == "self_attn.q_norm.weight") return set(L.q_norm, kHeadDim);
+    if (rest == "self_attn.k_norm.weight") return set(L.k_norm, kHeadDim);
+    if (rest == "self_attn.q_proj.weight") return set(L.w_qkv, (uint64_t)qh * kHeadDim * H);
+    if (rest == "self_attn.k_proj.weight") return set(L.w_qkv + (size_t)qh * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
+    if (rest == "self_attn.v_proj.weight")
+        return set(L.w_qkv + (size_t)(qh + kvh) * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
+    if (rest == "self_attn.o_proj.weight") return set(L.w_o, (uint64_t)H * qh * kHeadDim);
+    if (rest == "mlp.down_proj.weight") return set(L.w_down, (uint64_t)H * I);
+    if (rest == "mlp.gate_proj.weight") return set(L.w_gu, (uint64_t)I * H, 0);
+    if (rest == "mlp.up_proj.weight") return set(L.w_gu, (uint64_t)I * H, 64);
+    return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name");
+}
+
+// Copies rows [r0, r0 + rows) of a resolved weight from host memory `src` (rows x H bf16, or the whole flat tensor
+// when not interleaved: r0 / rows then count elements) on `st`; rows is a multiple of 64 for gate/up.
+static cudaError_t copy_weight_part(lrm_qwen Q, const WeightDst &w, uint64_t first, uint64_t n, const void *src,
+                                    cudaStream_t st) {
+    if (w.interleave < 0) return cudaMemcpyAsync(w.dst + first, src, n * 2, cudaMemcpyHostToDevice, st);
+    const size_t H = (size_t)Q->c.hidden;
+    const size_t r0 = first / H, rows = n / H;
+    return cudaMemcpy2DAsync(w.dst + ((r0 / 64) * 128 + (size_t)w.interleave) * H, 128 * H * 2, src, 64 * H * 2,
+                             64 * H * 2, rows / 64, cudaMemcpyHostToDevice, st);
+}
+
 lrm_status lrm_qwen_set_weight(lrm_qwen Q, const char *name, const uint16_t *w, uint64_t count) {
     if (!Q || !name || !w) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
     cudaSetDevice(Q->device);
-    const lrm_qwen_config &c = Q->c;
-    const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
-    std::string n(name);
-    auto put = [&](void *dst, uint64_t expect) -> lrm_status {
-        if (count != expect) return qfail(Q, LRM_ERR_ARGUMENT, n + ": wrong element count");
-        QTRY(Q, cudaMemcpy(dst, w, count * 2, cudaMemcpyHostToDevice), "set_weight");
-        return LRM_OK;
-    };
-    if (n == "model.embed_tokens.weight") return put(Q->embed, (uint64_t)c.vocab * H);
-    if (n == "model.norm.weight") return put(Q->final_norm, H);
-    int layer = -1, consumed = 0;
-    if (sscanf(name, "model.layers.%d.%n", &layer, &consumed) != 1 || consumed == 0 || layer < 0 || layer >= c.layers)
-        return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name of this model");
-    Layer &L = Q->layers[layer];
-    std::string rest = n.substr(consumed);
-    if (rest == "input_layernorm.weight") return put(L.in_norm, H);
-    if (rest == "post_attention_layernorm.weight") return put(L.post_norm, H);
-    if (rest == "self_attn.q_norm.weight") return put(L.q_norm, kHeadDim);
-    if (rest == "self_attn.k_norm.weight") return put(L.k_norm, kHeadDim);
-    if (rest == "self_attn.q_proj.weight") return put(L.w_qkv, (uint64_t)qh * kHeadDim * H);
-    if (rest == "self_attn.k_proj.weight") return put(L.w_qkv + (size_t)qh * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
-    if (rest == "self_attn.v_proj.weight")
-        return put(L.w_qkv + (size_t)(qh + kvh) * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
-    if (rest == "self_attn.o_proj.weight") return put(L.w_o, (uint64_t)H * qh * kHeadDim);
-    if (rest == "mlp.down_proj.weight") return put(L.w_down, (uint64_t)H * I);
-    if (rest == "mlp.gate_proj.weight" || rest == "mlp.up_proj.weight") {
-        if (count != (uint64_t)I * H) return qfail(Q, LRM_ERR_ARGUMENT, n + ": wrong element count");
-        const int off = rest == "mlp.gate_proj.weight" ? 0 : 64;
-        // rows j of gate/up go to row (j / 64) * 128 + off + j % 64: 64-row blocks, interleaved.
-        QTRY(Q, cudaMemcpy2D(L.w_gu + (size_t)off * H, (size_t)128 * H * 2, w, (size_t)64 * H * 2, (size_t)64 * H * 2,
-                             I / 64, cudaMemcpyHostToDevice),
-             "set_weight");
-        return LRM_OK;
+    WeightDst d;
+    LTRY(resolve_weight(Q, name, d));
+    if (count != d.count) return qfail(Q, LRM_ERR_ARGUMENT, std::string(name) + ": wrong element count");
+    QTRY(Q, copy_weight_part(Q, d, 0, count, w, Q->stream), "set_weight");
+    QTRY(Q, cudaStreamSynchronize(Q->stream), "set_weight");
+    return LRM_OK;
+}
+
+// bf16 bits of x rounded to nearest even (NaN stays a quiet NaN of the same sign).
+static inline uint16_t narrow_bf16(uint32_t u) {
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40u);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+lrm_status lrm_qwen_load_safetensors(lrm_qwen Q, const char *path, int32_t *loaded) {
+    if (!Q || !path) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
+    if (loaded) *loaded = 0;
+    cudaSetDevice(Q->device);
+    lrm_st_file f = nullptr;
+    lrm_status s = lrm_st_open(path, &f);
+    if (s != LRM_OK) {
+        Q->error = thread_error();
+        return s;
     }
-    return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name");
+    std::unique_ptr<lrm_st_file_s, lrm_status (*)(lrm_st_file)> guard(f, lrm_st_close);
+    int64_t count = 0;
+    lrm_st_info(f, nullptr, nullptr, &count, nullptr, nullptr);
+    // Every tensor is checked before any byte is copied.
+    std::vector<WeightDst> dst((size_t)count);
+    std::vector<lrm_st_entry> ent((size_t)count);
+    for (int64_t i = 0; i < count; ++i) {
+        lrm_st_entry_at(f, i, &ent[(size_t)i]);
+        const lrm_st_entry &e = ent[(size_t)i];
+        LTRY(resolve_weight(Q, e.name, dst[(size_t)i]));
+        if (e.dtype != LRM_ST_BF16 && e.dtype != LRM_ST_F32)
+            return qfail(Q, LRM_ERR_ARGUMENT, std::string(e.name) + ": only BF16 and F32 weights are loaded");
+        const uint64_t elems = (e.end - e.begin) / (e.dtype == LRM_ST_BF16 ? 2 : 4);
+        if (elems != dst[(size_t)i].count)
+            return qfail(Q, LRM_ERR_ARGUMENT, std::string(e.name) + ": wrong element count");
+    }
+    // Two pinned 64 MiB buffers: one fills from the mapped file while the other's copy runs.
+    constexpr size_t kChunk = 64u << 20;
+    uint16_t *pin[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    auto cleanup = [&]() {
+        cudaStreamSynchronize(Q->stream);
+        for (int b = 0; b < 2; ++b) {
+            if (pin[b]) cudaFreeHost(pin[b]);
+            if (done[b]) cudaEventDestroy(done[b]);
+        }
+    };
+    for (int b = 0; b < 2; ++b) {
+        cudaError_t e = cudaMallocHost(&pin[b], kChunk);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            cleanup();
+            return qcuda(Q, e, "pinned staging");
+        }
+    }
+    const size_t H = (size_t)Q->c.hidden;
+    uint64_t part = 0;
+    for (int64_t i = 0; i < count; ++i) {
+        const lrm_st_entry &e = ent[(size_t)i];
+        const WeightDst &d = dst[(size_t)i];
+        // elements per chunk; whole 64-row blocks for the interleaved gate/up rows
+        uint64_t step = kChunk / 2;
+        if (d.interleave >= 0) step = step / (64 * H) * (64 * H);
+        for (uint64_t first = 0; first < d.count; first += step, ++part) {
+            const uint64_t n = std::min<uint64_t>(step, d.count - first);
+            const int b = (int)(part & 1);
+            cudaError_t ce = cudaEventSynchronize(done[b]);  // the last copy out of this buffer has finished
+            if (ce != cudaSuccess) {
+                cleanup();
+                return qcuda(Q, ce, "staging");
+            }
+            if (e.dtype == LRM_ST_BF16) {
+                memcpy(pin[b], (const uint16_t *)e.data + first, n * 2);
+            } else {
+                const uint32_t *src = (const uint32_t *)e.data + first;
+                for (uint64_t k = 0; k < n; ++k) {
+                    uint32_t u;
+                    memcpy(&u, src + k, 4);
+                    pin[b][k] = narrow_bf16(u);
+                }
+            }
+            ce = copy_weight_part(Q, d, first, n, pin[b], Q->stream);
+            if (ce == cudaSuccess) ce = cudaEventRecord(done[b], Q->stream);
+            if (ce != cudaSuccess) {
+                cleanup();
+                return qcuda(Q, ce, (std::string("loading ") + e.name).c_str());
+            }
+        }
+        if (loaded) *loaded = (int32_t)(i + 1);
+    }
+    cleanup();
+    QTRY(Q, cudaGetLastError(), "loading the checkpoint");
+    return LRM_OK;
 }
 
 lrm_status lrm_qwen_set_rope(lrm_qwen Q, const float *cs, const float *sn, int32_t rows, int32_t half) {

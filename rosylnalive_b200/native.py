@@ -27,7 +27,12 @@ class CudaTimeoutError(TimeoutError):
 
 
 LRM_OK, LRM_ERR_CONTRACT, LRM_ERR_CUDA, LRM_ERR_TIMEOUT, LRM_ERR_ARGUMENT, LRM_ERR_OUT_OF_MEMORY, LRM_ERR_STATE, \
-    LRM_ERR_NO_DEVICE = range(8)
+    LRM_ERR_NO_DEVICE, LRM_ERR_FORMAT = range(9)
+
+
+class SafetensorsFormatError(ValueError):
+    """A file breaks the safetensors format (LRM_ERR_FORMAT): the reference's SafetensorsFormatException
+    (src/Lrm.Tensor/Safetensors.fs:16). The message names the file."""
 
 LRM_CUDA_DEBUG = 0x1
 LRM_CUDA_TIME_DISPATCHES = 0x2
@@ -127,6 +132,8 @@ def check(status: int, dev=None, what: str = ""):
         raise LookupError(msg)
     if status == LRM_ERR_OUT_OF_MEMORY:
         raise MemoryError(msg)
+    if status == LRM_ERR_FORMAT:
+        raise SafetensorsFormatError(msg)
     raise CudaDeviceError(msg)
 
 

@@ -44,6 +44,7 @@ N.extra_signatures({
     "lrm_qwen_sync": [P],
     "lrm_qwen_stream": [P, ctypes.POINTER(P)],
     "lrm_qwen_seq_len": [P, I32, PI32],
+    "lrm_qwen_load_safetensors": [P, ctypes.c_char_p, PI32],
 })
 
 
@@ -52,9 +53,11 @@ def _p(a: np.ndarray, t):
 
 
 class QwenEngine:
-    """One device's Qwen3 engine. `weights` maps HF names to bf16 bit arrays (uint16)."""
+    """One device's Qwen3 engine. `weights` maps HF names to bf16 bit arrays (uint16), or is the path (or a list of
+    paths) of safetensors checkpoint files holding every weight of the model once (BF16, or F32 narrowed to bf16),
+    streamed to the device by the library's reader."""
 
-    def __init__(self, cfg: QwenConfig, weights: dict, rope_cos: np.ndarray, rope_sin: np.ndarray, device: int = 0,
+    def __init__(self, cfg: QwenConfig, weights, rope_cos: np.ndarray, rope_sin: np.ndarray, device: int = 0,
                  max_seqs: int = 64, kv_pages: int | None = None, max_tokens: int = 4096, max_batch: int = 64,
                  max_pos: int | None = None):
         self.cfg = cfg
@@ -67,22 +70,55 @@ class QwenEngine:
         N.check(N.lib().lrm_qwen_create(device, ctypes.byref(c), ctypes.byref(h)), None, "lrm_qwen_create")
         self._h = h
         self.max_seqs, self.max_tokens, self.max_batch, self.max_pos = max_seqs, max_tokens, max_batch, max_pos
-        for name, shape in weight_shapes(cfg).items():
-            w = np.ascontiguousarray(weights[name], np.uint16)
-            if w.shape != tuple(shape):
-                raise ValueError(f"{name} is {w.shape}, expected {shape}")
-            self._check(N.lib().lrm_qwen_set_weight(self._h, name.encode(), _p(w, ctypes.c_uint16), w.size),
-                        "set_weight")
-        cos = np.ascontiguousarray(rope_cos[:max_pos], np.float32)
-        sin = np.ascontiguousarray(rope_sin[:max_pos], np.float32)
-        if cos.shape[0] < max_pos:
-            raise ValueError("the RoPE table has fewer rows than max_pos")
-        self._check(N.lib().lrm_qwen_set_rope(self._h, _p(cos, F32), _p(sin, F32), cos.shape[0], cos.shape[1]),
-                    "set_rope")
+        try:
+            if isinstance(weights, dict):
+                for name, shape in weight_shapes(cfg).items():
+                    w = np.ascontiguousarray(weights[name], np.uint16)
+                    if w.shape != tuple(shape):
+                        raise ValueError(f"{name} is {w.shape}, expected {shape}")
+                    self._check(N.lib().lrm_qwen_set_weight(self._h, name.encode(), _p(w, ctypes.c_uint16), w.size),
+                                "set_weight")
+            else:
+                self.load_checkpoint([weights] if isinstance(weights, (str, bytes)) or hasattr(weights, "__fspath__")
+                                     else list(weights))
+            cos = np.ascontiguousarray(rope_cos[:max_pos], np.float32)
+            sin = np.ascontiguousarray(rope_sin[:max_pos], np.float32)
+            if cos.shape[0] < max_pos:
+                raise ValueError("the RoPE table has fewer rows than max_pos")
+            self._check(N.lib().lrm_qwen_set_rope(self._h, _p(cos, F32), _p(sin, F32), cos.shape[0], cos.shape[1]),
+                        "set_rope")
+        except BaseException:
+            self.close()  # a half-built engine frees its device memory
+            raise
 
     def _check(self, status, what):
         if status != N.LRM_OK:
             N.check(status, None, what)
+
+    def load_safetensors(self, path) -> int:
+        """Streams every tensor of one safetensors file into the engine; returns how many it loaded."""
+        n = I32()
+        self._check(N.lib().lrm_qwen_load_safetensors(self._h, str(path).encode("utf-8"), ctypes.byref(n)),
+                    "load_safetensors")
+        return int(n.value)
+
+    def load_checkpoint(self, paths) -> None:
+        """Loads a checkpoint split over `paths`; every weight of the model must come exactly once."""
+        from .safetensors import SafetensorsFile
+
+        want = set(weight_shapes(self.cfg))
+        seen = set()
+        for p in paths:
+            with SafetensorsFile.open(p) as f:
+                names = set(f.names)
+            dup, extra = names & seen, names - want
+            if dup or extra:
+                raise ValueError(f"{p}: " + (f"tensors loaded twice: {sorted(dup)[:3]}" if dup else
+                                             f"not weights of this model: {sorted(extra)[:3]}"))
+            seen |= names
+            self.load_safetensors(p)
+        if seen != want:
+            raise ValueError(f"the checkpoint misses {len(want - seen)} weights, e.g. {sorted(want - seen)[:3]}")
 
     def close(self):
         if self._h:

@@ -8,7 +8,8 @@ Source: the reference's goldens/tiny/g1 set (README "The tiny set"): HF-named bf
 the pinned RoPE inverse frequencies and T_spec table (rope.safetensors), torch32 (fwd_f32.*) and torch64p (fwd_f64p.*)
 forward taps for prompts p0 (T=13) and p1 (T=1), logits for p2 (T=70) and the 64-step greedy ids and margins
 (greedy.safetensors). Nothing is recomputed: the arrays are copied as they are, bit for bit, so the tests can run
-where the reference is absent (the GPU box).
+where the reference is absent (the GPU box). The model file is also copied whole (tiny_g1_model.safetensors, checked
+against the reference's SHA256SUMS) for the safetensors reader's tests.
 """
 
 from __future__ import annotations
@@ -62,9 +63,26 @@ def main(reference_root: str) -> None:
         arrays["greedy/" + k] = v
     for pr in manifest["prompts"]:
         arrays["prompt/" + pr["name"]] = np.array(pr["ids"], np.int64)
-    out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tiny_g1.npz")
+    here = os.path.dirname(os.path.abspath(__file__))
+    out = os.path.join(here, "tiny_g1.npz")
     np.savez_compressed(out, **arrays)
     print(f"wrote {out}: {len(arrays)} arrays, {os.path.getsize(out)} bytes")
+    # The model file itself, byte for byte, for the safetensors reader's tests; its SHA-256 must be the one the
+    # reference's goldens/tiny/g1/model/SHA256SUMS lists.
+    import hashlib
+    import shutil
+
+    src = os.path.join(g, "model", "model.safetensors")
+    with open(os.path.join(g, "model", "SHA256SUMS")) as f:
+        want = next(ln.split()[0] for ln in f if ln.strip().endswith("model.safetensors"))
+    with open(src, "rb") as f:
+        got = hashlib.sha256(f.read()).hexdigest()
+    if got != want:
+        raise SystemExit(f"{src}: SHA-256 {got}, SHA256SUMS says {want}")
+    dst = os.path.join(here, "tiny_g1_model.safetensors")
+    shutil.copyfile(src, dst)
+    os.chmod(dst, 0o644)
+    print(f"copied {src} -> {dst} (SHA-256 {got})")
 
 
 if __name__ == "__main__":

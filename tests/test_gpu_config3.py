@@ -102,3 +102,29 @@ def test_config3_fp32_catalog_path_teacher_forced(config3):
     assert np.max(np.abs(got - ref_logits)) <= 1e-4
     decided = top2_margin(ref_logits) > 1e-3
     assert np.array_equal(np.array(ids)[decided], ref_ids[decided])
+
+
+def test_config3_checkpoint_streams_to_the_same_logits(config3, tmp_path):
+    # The full-size model (1.19 GB of bf16) written as a safetensors checkpoint and loaded by the library's streaming
+    # reader gives the same prefill logits, bit for bit, as the weights set from arrays.
+    import time
+
+    from rosylnalive_b200 import safetensors as ST
+
+    cfg, weights, cos, sin, prompt, ref_ids, ref_logits = config3
+    path = str(tmp_path / "model.safetensors")
+    ST.write(path, {n: ("BF16", w) for n, w in weights.items()})
+    t0 = time.time()
+    eng = Qw.QwenEngine(cfg, path, cos, sin, max_seqs=1, max_tokens=PROMPT, max_batch=1)
+    load_s = time.time() - t0
+    try:
+        _, got = eng.prefill([0], [prompt[:64]], want_logits=True)
+    finally:
+        eng.close()
+    eng = Qw.QwenEngine(cfg, weights, cos, sin, max_seqs=1, max_tokens=PROMPT, max_batch=1)
+    try:
+        _, want = eng.prefill([0], [prompt[:64]], want_logits=True)
+    finally:
+        eng.close()
+    assert np.array_equal(got, want)
+    print(f"checkpoint load incl. engine creation: {load_s:.2f} s for {sum(w.nbytes for w in weights.values()) / 1e9:.2f} GB")

@@ -80,6 +80,36 @@ def test_long_prefill_on_cta_pairs_matches_oracle(mini):
         eng.close()
 
 
+def test_checkpoint_loader_matches_set_weight(mini, tmp_path):
+    # The same weights through the library's safetensors loader: half of them in a BF16 file, half in an F32 file
+    # (exact widenings of the same bf16 values, so the loader's round-to-nearest-even narrowing must give them back);
+    # the prefill logits must be bit for bit those of the engine whose weights were set from arrays.
+    from rosylnalive_b200 import safetensors as ST
+
+    cfg, om, eng = mini
+    weights = S.random_weights(cfg, seed=0)
+    cos, sin = R.t_spec(R.torch_inv_freq_bits(cfg.rope_theta, cfg.head_dim), cfg.max_pos)
+    names = sorted(weights)
+    a, b = str(tmp_path / "a.safetensors"), str(tmp_path / "b.safetensors")
+    ST.write(a, {n: ("BF16", weights[n]) for n in names[::2]}, {"format": "pt"})
+    ST.write(b, {n: ("F32", (weights[n].astype(np.uint32) << 16).view(np.float32)) for n in names[1::2]})
+    eng2 = Qw.QwenEngine(cfg, [a, b], cos, sin, max_seqs=8, max_tokens=1024, max_batch=8)
+    try:
+        prompts = [S.random_prompt(cfg.vocab, n, seed=50 + i, stream=f"ck{i}") for i, n in enumerate((37, 90))]
+        n1, l1 = eng.prefill([0, 1], prompts, want_logits=True)
+        n2, l2 = eng2.prefill([0, 1], prompts, want_logits=True)
+        assert np.array_equal(n1, n2) and np.array_equal(l1, l2)
+        # refused: a tensor that is not a weight of this model, and a checkpoint that misses weights
+        c = str(tmp_path / "c.safetensors")
+        ST.write(c, {"lm_head.weight": ("BF16", weights["model.embed_tokens.weight"])})
+        with pytest.raises(ValueError):
+            eng2.load_safetensors(c)
+        with pytest.raises(ValueError):
+            Qw.QwenEngine(cfg, [a], cos, sin, max_seqs=2, max_tokens=64, max_batch=2).close()
+    finally:
+        eng2.close()
+
+
 def test_greedy_decode_matches_oracle(mini):
     cfg, om, eng = mini
     prompts = [S.random_prompt(cfg.vocab, n, seed=10 + i, stream=f"g{i}") for i, n in enumerate((16, 40, 5))]
