@@ -356,6 +356,53 @@ lrm_status lrm_st_entry_at(lrm_st_file f, int64_t index, lrm_st_entry *out);
 lrm_status lrm_st_find(lrm_st_file f, const char *name, lrm_st_entry *out);
 lrm_status lrm_st_metadata_at(lrm_st_file f, int64_t index, const char **key, const char **value);
 
+/* ---- tokenizer (host; needs no GPU) --------------------------------------------------------------------------
+ * The Qwen3 byte-level BPE tokenizer on the ends of the path (src/Lrm.Tokenizer/QwenTokenizer.fs:19-235): exact id
+ * parity with HF tokenizers 0.23.3 on Qwen3's tokenizer.json. Text crosses the ABI as UTF-8. Calls that produce a
+ * variable-length result take (out, cap, count): out null asks for the count only; a cap below the count is
+ * LRM_ERR_ARGUMENT with nothing written. A handle is immutable apart from its piece cache, and every call on it is
+ * safe from many threads at once. */
+typedef struct lrm_tokenizer_s *lrm_tokenizer;
+
+/* QwenTokenizer.fromJson (QwenTokenizer.fs:237-309, TokenizerJson.fs:219-250): parses and checks tokenizer.json.
+ * Anything but Qwen3's configuration (NFC, the exact Split regex, ByteLevel without prefix space or regex, plain
+ * BPE, added tokens matched on the raw text) is LRM_ERR_FORMAT with the reference's "tokenizer.json: ..." message. */
+lrm_status lrm_tok_parse(const void *json, uint64_t json_bytes, lrm_tokenizer *out);
+lrm_status lrm_tok_free(lrm_tokenizer t);
+/* VocabSize (vocabulary + added tokens), MergeCount, AddedTokens.Length (QwenTokenizer.fs:85-91). */
+lrm_status lrm_tok_info(lrm_tokenizer t, int32_t *vocab_size, int32_t *merges, int32_t *added);
+/* ClearCache and CachedPieces (QwenTokenizer.fs:218-222): the piece cache holds two generations of at most 32,768
+ * pieces or 1 Mi UTF-16 units each; pieces over 65,536 units are never cached; it never changes a result. */
+lrm_status lrm_tok_clear_cache(lrm_tokenizer t);
+lrm_status lrm_tok_cached_pieces(lrm_tokenizer t, int64_t *pieces);
+/* The i-th added token by id; `content` stays valid until lrm_tok_free. */
+lrm_status lrm_tok_added_at(lrm_tokenizer t, int32_t i, int32_t *id, const char **content, int32_t *special);
+/* Encode (QwenTokenizer.fs:97): LRM_ERR_ARGUMENT when `utf8` is not valid UTF-8 (the reference's lone-surrogate
+ * refusal; surrogates cannot be encoded in valid UTF-8). Adds no BOS or EOS. */
+lrm_status lrm_tok_encode(lrm_tokenizer t, const char *utf8, uint64_t n, int32_t *ids, uint64_t cap,
+                          uint64_t *count);
+/* EncodeBytes (QwenTokenizer.fs:130): `bytes` decoded with one U+FFFD per maximal invalid subpart, then Encode. */
+lrm_status lrm_tok_encode_bytes(lrm_tokenizer t, const uint8_t *bytes, uint64_t n, int32_t *ids, uint64_t cap,
+                                uint64_t *count);
+/* DecodeBytes (QwenTokenizer.fs:139): ids from VocabSize to 151,935 add nothing; an id below 0 or at 151,936 and
+ * above is LRM_ERR_ARGUMENT. */
+lrm_status lrm_tok_decode_bytes(lrm_tokenizer t, const int32_t *ids, uint64_t n, uint8_t *out, uint64_t cap,
+                                uint64_t *len);
+/* Decode (QwenTokenizer.fs:195): DecodeBytes as UTF-8 with one U+FFFD per maximal invalid subpart. */
+lrm_status lrm_tok_decode(lrm_tokenizer t, const int32_t *ids, uint64_t n, char *out, uint64_t cap, uint64_t *len);
+/* IdOf (QwenTokenizer.fs:200): an added token's content or a byte-level vocabulary string; -1 when there is none. */
+lrm_status lrm_tok_id_of(lrm_tokenizer t, const char *token, int32_t *id);
+/* TokenOf (QwenTokenizer.fs:209): `found` 0 for ids that have no token. */
+lrm_status lrm_tok_token_of(lrm_tokenizer t, int32_t id, char *out, uint64_t cap, uint64_t *len, int32_t *found);
+/* The stages on their own: Nfc.normalize (Nfc.fs), PreTokenizer.split (PreTokenizer.fs) as the byte offsets where
+ * pieces end, CharClass.ofScalar (CharClass.fs; 0 letter, 1 number, 2 white space, 3 other, -1 past U+10FFFF), the
+ * letter a scalar stands for in (?i:'s|'t|'re|'ve|'m|'ll|'d) (0 for none), and ByteLevel.charOf (ByteLevel.fs). */
+lrm_status lrm_tok_nfc(const char *utf8, uint64_t n, char *out, uint64_t cap, uint64_t *len);
+lrm_status lrm_tok_split(const char *utf8, uint64_t n, uint64_t *ends, uint64_t cap, uint64_t *count);
+int32_t lrm_tok_char_class(uint32_t scalar);
+int32_t lrm_tok_contraction_letter(uint32_t scalar);
+uint32_t lrm_tok_byte_char(uint8_t byte);
+
 /* ---- host helpers ------------------------------------------------------------------------------------------- */
 
 /* T_spec (src/Lrm.Tensor.CpuReference/Rope.fs:163-251): cos/sin [max_pos, half] float32 with

@@ -32,6 +32,7 @@ SOURCES = [
     "qwen_engine.cu",
     "decode_attn_static.cu",
     "safetensors.cpp",
+    "tokenizer.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -116,7 +116,7 @@ def last_error(dev=None) -> str:
     return buf.value.decode(errors="replace")
 
 
-def check(status: int, dev=None, what: str = ""):
+def check(status: int, dev=None, what: str = "", format_error=None):
     if status == LRM_OK:
         return
     msg = last_error(dev)
@@ -133,7 +133,7 @@ def check(status: int, dev=None, what: str = ""):
     if status == LRM_ERR_OUT_OF_MEMORY:
         raise MemoryError(msg)
     if status == LRM_ERR_FORMAT:
-        raise SafetensorsFormatError(msg)
+        raise (format_error or SafetensorsFormatError)(msg)
     raise CudaDeviceError(msg)
 
 

@@ -9,11 +9,13 @@ the pinned RoPE inverse frequencies and T_spec table (rope.safetensors), torch32
 forward taps for prompts p0 (T=13) and p1 (T=1), logits for p2 (T=70) and the 64-step greedy ids and margins
 (greedy.safetensors). Nothing is recomputed: the arrays are copied as they are, bit for bit, so the tests can run
 where the reference is absent (the GPU box). The model file is also copied whole (tiny_g1_model.safetensors, checked
-against the reference's SHA256SUMS) for the safetensors reader's tests.
+against the reference's SHA256SUMS) for the safetensors reader's tests, and the tokenizer oracle's Unicode and split
+probes (tokenizer_unicode-oracle.json, tokenizer_split-cases.jsonl).
 """
 
 from __future__ import annotations
 
+import gzip
 import json
 import os
 import struct
@@ -83,6 +85,38 @@ def main(reference_root: str) -> None:
     shutil.copyfile(src, dst)
     os.chmod(dst, 0o644)
     print(f"copied {src} -> {dst} (SHA-256 {got})")
+    # The tokenizer oracle's probes that need no tokenizer.json (tests/Lrm.Tokenizer.Tests/oracle, pinned by the
+    # SHA-256s of docs/contracts/tokenizer.md "Vectors"): Unicode classes, contraction letters, NFC split points and
+    # probe digests, and 4,000 pre-tokenizer split cases.
+    for name, want in (("unicode-oracle.json", "f9339ab0e55acabd0509b4f562ae831d97d167398aaeacbd47c4a49324acbb89"),
+                       ("split-cases.jsonl", "39bb2555c870896ecb4bc4c907c90a1dcb912aaf8ed75a143aee114c35bb3b95")):
+        src = os.path.join(reference_root, "tests", "Lrm.Tokenizer.Tests", "oracle", name)
+        with open(src, "rb") as f:
+            data = f.read()
+        got = hashlib.sha256(data).hexdigest()
+        if got != want:
+            raise SystemExit(f"{src}: SHA-256 {got}, the tokenizer contract pins {want}")
+        dst = os.path.join(here, "tokenizer_" + name)
+        with open(dst, "wb") as f:
+            f.write(data)
+        print(f"copied {src} -> {dst} (SHA-256 {got})")
+    # The id vectors that need the real tokenizer.json (the 1,800 oracle probe cases and O1's 5,597-case corpus,
+    # goldens/tokenizer/g1), gzip-compressed with a zero timestamp; the tests check the SHA-256 of the content.
+    for src_rel, name, want in (
+            ("tests/Lrm.Tokenizer.Tests/oracle/encode-cases.jsonl", "tokenizer_encode-cases.jsonl.gz",
+             "3ce0e0e7473f4e6465b92ba3482c31682d61d7c48645b535a987940bdd6743dd"),
+            ("goldens/tokenizer/g1/cases.jsonl", "tokenizer_corpus-cases.jsonl.gz",
+             "35ff0c43a1bc4325588b1a22953f861784e4ca76e0f3f863a5f70ff9ceb16c66")):
+        src = os.path.join(reference_root, *src_rel.split("/"))
+        with open(src, "rb") as f:
+            data = f.read()
+        got = hashlib.sha256(data).hexdigest()
+        if got != want:
+            raise SystemExit(f"{src}: SHA-256 {got}, the tokenizer contract pins {want}")
+        dst = os.path.join(here, name)
+        with open(dst, "wb") as f:
+            f.write(gzip.compress(data, compresslevel=9, mtime=0))
+        print(f"copied {src} -> {dst} (SHA-256 of the content {got})")
 
 
 if __name__ == "__main__":
