@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--no-decode", action="store_true", help="only the config-4 prefill part")
     p.add_argument("--prefill-batch", type=int, default=16, help="config-4 prompts per job")
     p.add_argument("--prefill-len", type=int, default=2048, help="config-4 prompt length")
+    p.add_argument("--pipeline", action="store_true",
+                   help="pipeline stage split instead of data parallelism: under torchrun each rank holds 28/N layers "
+                        "of every sequence (not the headline)")
+    p.add_argument("--microbatches", type=int, default=2, help="--pipeline: sequence groups in flight")
     p.add_argument("--op-bench", action="store_true",
                    help="operator benchmarks only (config 2 attention, config 4 GEMM shapes); one JSON line")
     return p.parse_args()
@@ -349,6 +353,58 @@ def run_ours(args, dist):
         print(json.dumps(line), flush=True)
 
 
+def run_pipeline(args, dist):
+    """The pipeline stage split (SURVEY-scope row "serving / pipeline stage split"; not the headline): rank r holds
+    stage r of the 28 layers (rosylnalive_b200.pipeline.split_layers) for all B x N sequences; the fp32 residual
+    crosses ranks with NCCL send/recv, the next ids return to rank 0, and the sequences run in `microbatches` groups
+    so the stages work concurrently. Setup prefills the KV caches through the same pipeline; the timed region is
+    K decode steps of every group, timed on rank 0's device with a barrier and max over ranks."""
+    import torch
+
+    from rosylnalive_b200 import pipeline as PL
+    from rosylnalive_b200 import qwen as Qw
+    from rosylnalive_b200 import rope as R
+    from rosylnalive_b200 import synthetic as S
+
+    cfg = S.QWEN3_0_6B
+    N, B, ctx, K, W = dist.world, args.batch * dist.world, args.context, args.steps, args.warmup
+    first, end = PL.split_layers(cfg.layers, N)[dist.rank]
+    max_pos = (ctx + W + K + 16 + 15) // 16 * 16
+    cos, sin = R.t_spec(R.QWEN3_INV_FREQ_BITS, max_pos)
+    weights = {k: v for k, v in S.random_weights(cfg, seed=0).items()}
+    groups = max(1, args.microbatches)
+    per_group = (B + groups - 1) // groups
+    eng = Qw.QwenEngine(cfg, weights, cos, sin, device=dist.local, max_seqs=B, max_tokens=32768,
+                        max_batch=per_group, max_pos=max_pos, stage=(first, end))
+    dev = f"cuda:{dist.local}"
+    pipe = PL.DistPipeline(eng, dist.rank, N, dev)
+    prompts = list(S.random_prompts(cfg.vocab, B, ctx, seed=1000))
+    # setup: prefill (in groups of at most 32,768 tokens) and W warm-up steps through the pipeline
+    t0 = time.time()
+    pipe.prefill(prompts, microbatches=max(groups, (B * ctx + 32767) // 32768))
+    pipe.decode_steps(W, microbatches=groups)
+    setup_s = time.time() - t0
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ids = pipe.decode_steps(K, microbatches=groups)
+    e1.record()
+    e1.synchronize()
+    dist.barrier()
+    ms = dist.max(e0.elapsed_time(e1))
+    eng.close()
+    if dist.rank == 0:
+        print(json.dumps({"metric": METRIC, "value": B * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": N,
+                          "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": f"config5 decode through a {N}-stage pipeline: {B} sequences, "
+                                                 f"{ctx}-token paged KV, {groups} microbatches",
+                                     "parallelism": f"pp{N} (layers {PL.split_layers(cfg.layers, N)})"},
+                          "mode": "pipeline", "setup_s": setup_s,
+                          "ids_checksum": int(np.sum(ids)) if ids is not None else None}), flush=True)
+
+
 def weights_bytes(cfg) -> int:
     from rosylnalive_b200.executor import weight_shapes
 
@@ -508,7 +564,10 @@ def main():
         return
     dist.init()
     try:
-        run_ours(args, dist)
+        if args.pipeline:
+            run_pipeline(args, dist)
+        else:
+            run_ours(args, dist)
     finally:
         dist.close()
 

@@ -255,6 +255,23 @@ typedef struct lrm_qwen_config {
 } lrm_qwen_config;
 
 lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *config, lrm_qwen *out);
+
+/* A pipeline stage (the reference's stage split, docs/dev-plan.md "StagePipeline": stage 0 runs embed plus layers
+ * 0-13, stage 1 layers 14-27 and the head, with the fp32 residual crossing between them): an engine holding layers
+ * [first_layer, end_layer) of the `config->layers`-layer model and their KV cache. The first stage (first_layer 0)
+ * embeds ids; the last (end_layer == layers) applies the final norm and the tied head; set_weight and
+ * load_safetensors skip the weights of other stages. Prefill and decode on a stage:
+ *  - a stage that is not the first reads its input residual from rows [0, T) of lrm_qwen_residual (T = the call's
+ *    tokens, in the call's order), which the caller writes before the call (ordered on lrm_qwen_stream or
+ *    synchronised); `ids` may be NULL;
+ *  - a stage that is not the last leaves its output residual in the same rows; `next_ids` and `logits` may be NULL.
+ * The split forward is bit-identical to the unsplit one. lrm_qwen_create is lrm_qwen_create_stage(0, layers). */
+lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *config, int32_t first_layer,
+                                 int32_t end_layer, lrm_qwen *out);
+/* The stage's layer range. */
+lrm_status lrm_qwen_stage(lrm_qwen q, int32_t *first_layer, int32_t *end_layer);
+/* The device pointer of the fp32 residual x [rows][hidden] (rows = max(max_tokens, max_batch)). */
+lrm_status lrm_qwen_residual(lrm_qwen q, float **x, int64_t *rows);
 lrm_status lrm_qwen_destroy(lrm_qwen q);
 
 /* Copies one HF-named bf16 weight (e.g. "model.layers.3.self_attn.q_proj.weight") from host memory into the engine's

@@ -25,9 +25,14 @@ __host__ __device__ inline size_t kv_page_elems(int kv_heads) { return (size_t)k
 cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
                               const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st);
 
-// x[t] += sum_s partial[s][t] (splits >= 0; 0 = no add); xn[t] = bf16(rmsnorm(x[t]) * w).
+// x[t] += sum_s partial[s][t] (splits >= 0; 0 = no add); xn[t] = bf16(rmsnorm(x[t]) * w). With splits > 0 and w
+// null only the sum is written. splits 0 runs the warp-per-row form (prefill); splits > 0 the block-per-row form.
 cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
                               const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st);
+// xn[t] = bf16(rmsnorm(x[t]) * w) in the block-per-row form of launch_resid_norm, whose sum of squares has the same
+// order as a decode step's fused residual + norm (a pipeline stage resumes a decode step with it).
+cudaError_t launch_norm_rows_block(float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
+                                   __nv_bfloat16 *xn, cudaStream_t st);
 
 // From qkv = sum_s partial[s] ([T][q+2kv heads][128] fp32): q = rope(rmsnorm(q_head) * q_norm) -> q_out bf16,
 // k = rope(rmsnorm(k_head) * k_norm) and raw v -> bf16 into the paged cache at (tok_slot[t], tok_pos[t]) and, when

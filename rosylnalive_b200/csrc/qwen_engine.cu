@@ -19,6 +19,12 @@
 // Decode GEMMs swap A and B (weights fill the 128-row tensor-core tile, the B <= 64 tokens are N) and split K so
 // every weight matrix is streamed by ~128 CTAs; the consumers reduce the splits in a fixed order. The decode step is
 // a fixed sequence of launches over device-resident inputs, so it is captured once as a CUDA graph and replayed.
+//
+// A pipeline stage (lrm_qwen_create_stage) holds layers [first, end) of the model and their KV cache: the first
+// stage embeds ids, the last applies the final norm and the tied head; between stages the fp32 residual x crosses
+// (lrm_qwen_residual). A stage resumes with the norm form the unsplit forward uses at that point (warp rows in
+// prefill, block rows in decode) and ends with the residual sum alone, so a split forward is bit-identical to the
+// unsplit one.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
@@ -59,6 +65,8 @@ T *carve(uint8_t *&p, size_t n) {
 
 struct lrm_qwen_s {
     lrm_qwen_config c;
+    int first = 0, nl = 0;               // this stage's layers: [first, first + nl) of c.layers
+    bool is_first = true, is_last = true;  // embeds ids / applies the final norm and the head
     int device = 0;
     cudaStream_t stream = nullptr;
     int sms = 148;
@@ -175,6 +183,13 @@ struct PdlScope {
     ~PdlScope() { set_pdl(false); }
 };
 
+// The gain of the norm after local layer l: the next layer's input norm, the final norm after the model's last
+// layer, or null after the last layer of an earlier stage.
+static const __nv_bfloat16 *next_norm_of(lrm_qwen Q, int l) {
+    if (l + 1 < Q->nl) return Q->layers[l + 1].in_norm;
+    return Q->is_last ? Q->final_norm : nullptr;
+}
+
 static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
     PdlScope pdl;
     const lrm_qwen_config &c = Q->c;
@@ -182,13 +197,16 @@ static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
     const int nqkv = Q->qkv_rows;
     KTRY(Q, launch_advance(Q->d_slots, B, Q->d_seq_len, Q->tok_pos, st), "advance");
-    KTRY(Q, launch_embed_norm(Q->ids, B, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
-         "embed_norm");
+    if (Q->is_first)
+        KTRY(Q, launch_embed_norm(Q->ids, B, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
+             "embed_norm");
+    else  // x[0, B) holds the previous stage's residual
+        KTRY(Q, launch_norm_rows_block(Q->x, B, H, Q->layers[0].in_norm, c.eps, Q->xn, st), "norm");
     const int s_qkv = choose_splits((nqkv + 127) / 128, (H + 63) / 64, Q->sms);
     const int s_o = choose_splits((H + 127) / 128, (qh * kHeadDim + 63) / 64, Q->sms);
     const int s_gu = choose_splits((2 * I + 127) / 128, (H + 63) / 64, Q->sms);
     const int s_d = choose_splits((H + 127) / 128, (I + 63) / 64, Q->sms);
-    for (int l = 0; l < c.layers; ++l) {
+    for (int l = 0; l < Q->nl; ++l) {
         const Layer &L = Q->layers[l];
         LTRY(gemm(Q, L.w_qkv, Q->xn, nqkv, B, H, EPI_PARTIAL, 64, s_qkv, Q->partial, nqkv, nullptr, 0,
                   (size_t)B * nqkv));
@@ -236,10 +254,11 @@ static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
                   (size_t)B * 2 * I));
         KTRY(Q, launch_swiglu_reduce(Q->partial, s_gu, (size_t)B * 2 * I, B, I, Q->act, st), "swiglu_reduce");
         LTRY(gemm(Q, L.w_down, Q->act, H, B, I, EPI_PARTIAL, 64, s_d, Q->partial, H, nullptr, 0, (size_t)B * H));
-        const __nv_bfloat16 *next_norm = l + 1 < c.layers ? Q->layers[l + 1].in_norm : Q->final_norm;
+        const __nv_bfloat16 *next_norm = next_norm_of(Q, l);  // null: the stage ends with the residual
         KTRY(Q, launch_resid_norm(Q->x, Q->partial, s_d, (size_t)B * H, B, H, next_norm, c.eps, Q->xn, st),
              "resid_norm");
     }
+    if (!Q->is_last) return LRM_OK;
     LTRY(gemm(Q, Q->embed, Q->xn, c.vocab, B, H, EPI_PARTIAL, 64, 1, Q->partial, c.vocab, nullptr, 0,
               (size_t)B * c.vocab));
     KTRY(Q, launch_argmax(Q->partial, B, c.vocab, Q->next, st), "argmax");
@@ -277,6 +296,12 @@ static lrm_status upload_page_row(lrm_qwen Q, int slot) {
 extern "C" {
 
 lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *cfg, lrm_qwen *out) {
+    if (!cfg) return qfail(nullptr, LRM_ERR_ARGUMENT, "null argument");
+    return lrm_qwen_create_stage(device, cfg, 0, cfg->layers, out);
+}
+
+lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int32_t first_layer, int32_t end_layer,
+                                 lrm_qwen *out) {
     if (!cfg || !out) return qfail(nullptr, LRM_ERR_ARGUMENT, "null argument");
     *out = nullptr;
     const lrm_qwen_config c = *cfg;
@@ -288,10 +313,16 @@ lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *cfg, lrm_qwen 
     if (c.layers < 1 || c.vocab < 1 || c.max_pos < 1 || c.max_seqs < 1 || c.kv_pages < 1 || c.max_tokens < 1 ||
         c.max_batch < 1 || c.max_batch > 65535)
         return qfail(nullptr, LRM_ERR_ARGUMENT, "sizes must be positive");
+    if (first_layer < 0 || end_layer <= first_layer || end_layer > c.layers)
+        return qfail(nullptr, LRM_ERR_ARGUMENT, "a stage holds layers [first, end) with 0 <= first < end <= layers");
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return qcuda(nullptr, e, "cudaSetDevice");
     std::unique_ptr<lrm_qwen_s> Q(new lrm_qwen_s());
     Q->c = c;
+    Q->first = first_layer;
+    Q->nl = end_layer - first_layer;
+    Q->is_first = first_layer == 0;
+    Q->is_last = end_layer == c.layers;
     Q->device = device;
     Q->err = device_error_word();
     Q->sms = device_sms();
@@ -302,14 +333,15 @@ lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *cfg, lrm_qwen 
     // weights
     size_t per_layer = (size_t)Q->qkv_rows * H + (size_t)H * qh * kHeadDim + (size_t)2 * I * H + (size_t)H * I +
                        2 * H + 2 * kHeadDim;
-    size_t wbytes = ((size_t)V * H + H) * 2 + (size_t)c.layers * (per_layer * 2 + 8 * 256) + 4096;
+    const bool has_embed = Q->is_first || Q->is_last;  // the gather table, and the tied head
+    size_t wbytes = ((has_embed ? (size_t)V * H : 0) + H) * 2 + (size_t)Q->nl * (per_layer * 2 + 8 * 256) + 4096;
     QTRY(Q.get(), cudaMalloc(&Q->wmem, wbytes), "weights");
     Q->wbytes = wbytes;
     QTRY(Q.get(), cudaMemset(Q->wmem, 0, wbytes), "weights");
     uint8_t *p = Q->wmem;
-    Q->embed = carve<__nv_bfloat16>(p, (size_t)V * H);
-    Q->final_norm = carve<__nv_bfloat16>(p, H);
-    Q->layers.resize(c.layers);
+    Q->embed = has_embed ? carve<__nv_bfloat16>(p, (size_t)V * H) : nullptr;
+    Q->final_norm = Q->is_last ? carve<__nv_bfloat16>(p, H) : nullptr;
+    Q->layers.resize(Q->nl);
     for (auto &L : Q->layers) {
         L.w_qkv = carve<__nv_bfloat16>(p, (size_t)Q->qkv_rows * H);
         L.w_o = carve<__nv_bfloat16>(p, (size_t)H * qh * kHeadDim);
@@ -325,9 +357,9 @@ lrm_status lrm_qwen_create(int32_t device, const lrm_qwen_config *cfg, lrm_qwen 
     // KV pool and page tables
     Q->maxp = (c.max_pos + kPageTokens - 1) / kPageTokens;
     Q->layer_pool_elems = (size_t)c.kv_pages * kv_page_elems(kvh);
-    e = cudaMalloc(&Q->pool, Q->layer_pool_elems * c.layers * sizeof(__nv_bfloat16));
+    e = cudaMalloc(&Q->pool, Q->layer_pool_elems * Q->nl * sizeof(__nv_bfloat16));
     if (e != cudaSuccess) return qfail(Q.get(), LRM_ERR_OUT_OF_MEMORY, "KV pool allocation failed");
-    QTRY(Q.get(), cudaMemset(Q->pool, 0, Q->layer_pool_elems * c.layers * sizeof(__nv_bfloat16)), "KV pool");
+    QTRY(Q.get(), cudaMemset(Q->pool, 0, Q->layer_pool_elems * Q->nl * sizeof(__nv_bfloat16)), "KV pool");
     QTRY(Q.get(), cudaMalloc(&Q->d_pages, sizeof(int32_t) * (size_t)c.max_seqs * Q->maxp), "pages");
     QTRY(Q.get(), cudaMemset(Q->d_pages, 0, sizeof(int32_t) * (size_t)c.max_seqs * Q->maxp), "pages");
     QTRY(Q.get(), cudaMalloc(&Q->d_seq_len, sizeof(int32_t) * c.max_seqs), "seq_len");
@@ -400,7 +432,7 @@ lrm_status lrm_qwen_destroy(lrm_qwen Q) {
 // rows j at row (j / 64) * 128 + interleave + j % 64 of w_gu (64-row blocks, so a 128-column GEMM tile holds matching
 // gate and up columns).
 struct WeightDst {
-    __nv_bfloat16 *dst = nullptr;
+    __nv_bfloat16 *dst = nullptr;  // null for a weight this stage does not hold
     uint64_t count = 0;
     int interleave = -1;
 };
@@ -420,16 +452,20 @@ static lrm_status resolve_weight(lrm_qwen Q, const std::string &n, WeightDst &w)
     if (sscanf(n.c_str(), "model.layers.%d.%n", &layer, &consumed) != 1 || consumed == 0 || layer < 0 ||
         layer >= c.layers)
         return qfail(Q, LRM_ERR_ARGUMENT, n + ": not a Qwen3 weight name of this model");
-    Layer &L = Q->layers[layer];
+    const bool held = layer >= Q->first && layer < Q->first + Q->nl;
+    static const Layer none{};
+    const Layer &L = held ? Q->layers[layer - Q->first] : none;
+    auto at = [&](__nv_bfloat16 *base, size_t off) { return base ? base + off : nullptr; };
     const std::string rest = n.substr(consumed);
     if (rest == "input_layernorm.weight") return set(L.in_norm, H);
     if (rest == "post_attention_layernorm.weight") return set(L.post_norm, H);
     if (rest == "self_attn.q_norm.weight") return set(L.q_norm, kHeadDim);
     if (rest == "self_attn.k_norm.weight") return set(L.k_norm, kHeadDim);
     if (rest == "self_attn.q_proj.weight") return set(L.w_qkv, (uint64_t)qh * kHeadDim * H);
-    if (rest == "self_attn.k_proj.weight") return set(L.w_qkv + (size_t)qh * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
+    if (rest == "self_attn.k_proj.weight")
+        return set(at(L.w_qkv, (size_t)qh * kHeadDim * H), (uint64_t)kvh * kHeadDim * H);
     if (rest == "self_attn.v_proj.weight")
-        return set(L.w_qkv + (size_t)(qh + kvh) * kHeadDim * H, (uint64_t)kvh * kHeadDim * H);
+        return set(at(L.w_qkv, (size_t)(qh + kvh) * kHeadDim * H), (uint64_t)kvh * kHeadDim * H);
     if (rest == "self_attn.o_proj.weight") return set(L.w_o, (uint64_t)H * qh * kHeadDim);
     if (rest == "mlp.down_proj.weight") return set(L.w_down, (uint64_t)H * I);
     if (rest == "mlp.gate_proj.weight") return set(L.w_gu, (uint64_t)I * H, 0);
@@ -454,6 +490,7 @@ lrm_status lrm_qwen_set_weight(lrm_qwen Q, const char *name, const uint16_t *w, 
     WeightDst d;
     LTRY(resolve_weight(Q, name, d));
     if (count != d.count) return qfail(Q, LRM_ERR_ARGUMENT, std::string(name) + ": wrong element count");
+    if (!d.dst) return LRM_OK;  // another pipeline stage's weight
     QTRY(Q, copy_weight_part(Q, d, 0, count, w, Q->stream), "set_weight");
     QTRY(Q, cudaStreamSynchronize(Q->stream), "set_weight");
     return LRM_OK;
@@ -515,6 +552,7 @@ lrm_status lrm_qwen_load_safetensors(lrm_qwen Q, const char *path, int32_t *load
     for (int64_t i = 0; i < count; ++i) {
         const lrm_st_entry &e = ent[(size_t)i];
         const WeightDst &d = dst[(size_t)i];
+        if (!d.dst) continue;  // another pipeline stage's weight
         // elements per chunk; whole 64-row blocks for the interleaved gate/up rows
         uint64_t step = kChunk / 2;
         if (d.interleave >= 0) step = step / (64 * H) * (64 * H);
@@ -543,7 +581,7 @@ lrm_status lrm_qwen_load_safetensors(lrm_qwen Q, const char *path, int32_t *load
                 return qcuda(Q, ce, (std::string("loading ") + e.name).c_str());
             }
         }
-        if (loaded) *loaded = (int32_t)(i + 1);
+        if (loaded) *loaded += 1;
     }
     cleanup();
     QTRY(Q, cudaGetLastError(), "loading the checkpoint");
@@ -594,7 +632,7 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
                             uint32_t *next_ids, float *logits) {
     LTRY(check_ready(Q));
     const lrm_qwen_config &c = Q->c;
-    if (nseq < 1 || nseq > c.max_seqs || !slots || !lens || !ids || !next_ids)
+    if (nseq < 1 || nseq > c.max_seqs || !slots || !lens || (Q->is_first && !ids) || (Q->is_last && !next_ids))
         return qfail(Q, LRM_ERR_ARGUMENT, "bad prefill arguments");
     std::vector<int32_t> cu(nseq + 1, 0), last(nseq), tslot, tpos;
     int max_len = 0;
@@ -617,10 +655,11 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         }
         Q->h_seq_len[slots[i]] = lens[i];
     }
-    for (int i = 0; i < T; ++i)
-        if (ids[i] >= (uint32_t)c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
+    if (Q->is_first)
+        for (int i = 0; i < T; ++i)
+            if (ids[i] >= (uint32_t)c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
     cudaStream_t st = Q->stream;
-    QTRY(Q, cudaMemcpyAsync(Q->ids, ids, 4 * (size_t)T, cudaMemcpyHostToDevice, st), "ids");
+    if (Q->is_first) QTRY(Q, cudaMemcpyAsync(Q->ids, ids, 4 * (size_t)T, cudaMemcpyHostToDevice, st), "ids");
     QTRY(Q, cudaMemcpyAsync(Q->tok_slot, tslot.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "slots");
     QTRY(Q, cudaMemcpyAsync(Q->tok_pos, tpos.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "positions");
     QTRY(Q, cudaMemcpyAsync(Q->cu, cu.data(), 4 * (size_t)(nseq + 1), cudaMemcpyHostToDevice, st), "cu_seqlens");
@@ -629,9 +668,12 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slots[i], &lens[i], 4, cudaMemcpyHostToDevice, st), "seq_len");
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
     PdlScope pdl;
-    KTRY(Q, launch_embed_norm(Q->ids, T, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
-         "embed_norm");
-    for (int l = 0; l < c.layers; ++l) {
+    if (Q->is_first)
+        KTRY(Q, launch_embed_norm(Q->ids, T, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
+             "embed_norm");
+    else  // x[0, T) holds the previous stage's residual
+        KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, Q->layers[0].in_norm, c.eps, Q->xn, st), "norm");
+    for (int l = 0; l < Q->nl; ++l) {
         const Layer &L = Q->layers[l];
         // q/k/v GEMM with QK-RMSNorm, RoPE and the paged KV append in its epilogue (no fp32 q/k/v round trip).
         QkvEpilogue qe;
@@ -667,9 +709,10 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, L.post_norm, c.eps, Q->xn, st), "resid_norm");
         LTRY(gemm(Q, Q->xn, L.w_gu, T, 2 * I, H, EPI_SWIGLU, 256, 1, Q->act, I, nullptr, 0, 0));
         LTRY(gemm(Q, Q->act, L.w_down, T, H, I, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
-        const __nv_bfloat16 *next_norm = l + 1 < c.layers ? Q->layers[l + 1].in_norm : Q->final_norm;
-        KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, next_norm, c.eps, Q->xn, st), "resid_norm");
+        if (const __nv_bfloat16 *next_norm = next_norm_of(Q, l))
+            KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, next_norm, c.eps, Q->xn, st), "resid_norm");
     }
+    if (!Q->is_last) return sync_check(Q);
     KTRY(Q, launch_gather_rows(Q->xn, Q->last_idx, nseq, H, Q->xl, st), "gather");
     LTRY(gemm(Q, Q->embed, Q->xl, c.vocab, nseq, H, EPI_PARTIAL, 64, 1, Q->partial, c.vocab, nullptr, 0,
               (size_t)nseq * c.vocab));
@@ -708,14 +751,17 @@ static lrm_status ensure_pages(lrm_qwen Q, int32_t batch, const int32_t *slots, 
 lrm_status lrm_qwen_decode(lrm_qwen Q, int32_t batch, const int32_t *slots, const uint32_t *ids, uint32_t *next_ids,
                            float *logits) {
     LTRY(check_ready(Q));
-    if (!ids || !next_ids) return qfail(Q, LRM_ERR_ARGUMENT, "null ids");
-    for (int b = 0; b < batch; ++b)
-        if (ids[b] >= (uint32_t)Q->c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
+    if ((Q->is_first && !ids) || (Q->is_last && !next_ids)) return qfail(Q, LRM_ERR_ARGUMENT, "null ids");
+    if (Q->is_first)
+        for (int b = 0; b < batch; ++b)
+            if (ids[b] >= (uint32_t)Q->c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
     LTRY(set_slots(Q, batch, slots));
     LTRY(ensure_pages(Q, batch, slots, 1));
     cudaStream_t st = Q->stream;
-    memcpy(Q->h_pinned, ids, 4 * (size_t)batch);
-    QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, st), "ids");
+    if (Q->is_first) {
+        memcpy(Q->h_pinned, ids, 4 * (size_t)batch);
+        QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, st), "ids");
+    }
     const bool use_graph = Q->graph && Q->graph_batch == batch &&
                            std::equal(Q->graph_slots.begin(), Q->graph_slots.end(), slots);
     if (use_graph) {
@@ -723,12 +769,15 @@ lrm_status lrm_qwen_decode(lrm_qwen Q, int32_t batch, const int32_t *slots, cons
     } else {
         LTRY(decode_step(Q, batch));
     }
-    QTRY(Q, cudaMemcpyAsync(Q->h_pinned + batch, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToHost, st), "next");
-    if (logits)
-        QTRY(Q, cudaMemcpyAsync(logits, Q->partial, 4 * (size_t)batch * Q->c.vocab, cudaMemcpyDeviceToHost, st),
-             "logits");
+    if (Q->is_last) {
+        QTRY(Q, cudaMemcpyAsync(Q->h_pinned + batch, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToHost, st),
+             "next");
+        if (logits)
+            QTRY(Q, cudaMemcpyAsync(logits, Q->partial, 4 * (size_t)batch * Q->c.vocab, cudaMemcpyDeviceToHost, st),
+                 "logits");
+    }
     LTRY(sync_check(Q));
-    memcpy(next_ids, Q->h_pinned + batch, 4 * (size_t)batch);
+    if (Q->is_last) memcpy(next_ids, Q->h_pinned + batch, 4 * (size_t)batch);
     for (int b = 0; b < batch; ++b) Q->h_seq_len[slots[b]] += 1;
     return LRM_OK;
 }
@@ -738,7 +787,7 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
     LTRY(check_ready(Q));
     const bool timed = flags & LRM_QWEN_GRAPH_TIME_ATTENTION;
     if (timed && Q->attn_ev.empty()) {
-        Q->attn_ev.resize(2 * Q->c.layers);
+        Q->attn_ev.resize(2 * Q->nl);
         for (auto &e : Q->attn_ev) QTRY(Q, cudaEventCreate(&e), "event");
     }
     LTRY(set_slots(Q, batch, slots));
@@ -754,7 +803,7 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
     cudaGraph_t g;
     QTRY(Q, cudaStreamBeginCapture(Q->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     lrm_status s = decode_step(Q, batch, timed);
-    if (s == LRM_OK) {
+    if (s == LRM_OK && Q->is_first && Q->is_last) {
         cudaError_t e = cudaMemcpyAsync(Q->ids, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToDevice, Q->stream);
         if (e != cudaSuccess) s = qcuda(Q, e, "feedback copy");
     }
@@ -810,7 +859,7 @@ lrm_status lrm_qwen_attention_ms(lrm_qwen Q, float *ms) {
     if (!Q->graph || !Q->graph_timed) return qfail(Q, LRM_ERR_STATE, "no timed decode graph captured");
     cudaSetDevice(Q->device);
     LTRY(sync_check(Q));
-    for (int l = 0; l < Q->c.layers; ++l)
+    for (int l = 0; l < Q->nl; ++l)
         QTRY(Q, cudaEventElapsedTime(&ms[l], Q->attn_ev[2 * l], Q->attn_ev[2 * l + 1]), "event time");
     return LRM_OK;
 }
@@ -836,6 +885,20 @@ lrm_status lrm_qwen_sync(lrm_qwen Q) {
 lrm_status lrm_qwen_stream(lrm_qwen Q, void **stream) {
     if (!Q || !stream) return LRM_ERR_ARGUMENT;
     *stream = (void *)Q->stream;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_residual(lrm_qwen Q, float **x, int64_t *rows) {
+    if (!Q || !x) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
+    *x = Q->x;
+    if (rows) *rows = Q->c.max_tokens > Q->c.max_batch ? Q->c.max_tokens : Q->c.max_batch;
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_stage(lrm_qwen Q, int32_t *first_layer, int32_t *end_layer) {
+    if (!Q || !first_layer || !end_layer) return qfail(Q, LRM_ERR_ARGUMENT, "null argument");
+    *first_layer = Q->first;
+    *end_layer = Q->first + Q->nl;
     return LRM_OK;
 }
 

@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(256) resid_norm_kernel(float *x, const float *
         if (splits) xr[c] = v;
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
+    if (!w) return;  // the residual sum alone (the last layer of a pipeline stage)
     const float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
     for (int c = threadIdx.x; c < n4; c += 256) {
         const float4 v = xr[c];
@@ -525,6 +526,12 @@ cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t
                              w, eps, xn);
     return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, partial, splits, split_stride, hidden, w,
                          eps, xn);
+}
+
+cudaError_t launch_norm_rows_block(float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
+                                  __nv_bfloat16 *xn, cudaStream_t st) {
+    return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, (const float *)nullptr, 0, (size_t)0,
+                         hidden, w, eps, xn);
 }
 
 cudaError_t launch_qk_norm_rope_kv(const QkvArgs &a, cudaStream_t st) {

@@ -28,6 +28,9 @@ PI32, PU32, PF32, PU16 = (ctypes.POINTER(t) for t in (I32, U32, F32, ctypes.c_ui
 
 N.extra_signatures({
     "lrm_qwen_create": [I32, ctypes.POINTER(QwenConfigC), ctypes.POINTER(P)],
+    "lrm_qwen_create_stage": [I32, ctypes.POINTER(QwenConfigC), I32, I32, ctypes.POINTER(P)],
+    "lrm_qwen_stage": [P, PI32, PI32],
+    "lrm_qwen_residual": [P, ctypes.POINTER(P), ctypes.POINTER(ctypes.c_int64)],
     "lrm_qwen_destroy": [P],
     "lrm_qwen_set_weight": [P, ctypes.c_char_p, PU16, U64],
     "lrm_qwen_set_rope": [P, PF32, PF32, I32, I32],
@@ -52,27 +55,61 @@ def _p(a: np.ndarray, t):
     return a.ctypes.data_as(ctypes.POINTER(t))
 
 
+def stage_weight_names(cfg: QwenConfig, first: int, end: int) -> list:
+    """The HF weight names a stage holding layers [first, end) loads: its layers' weights, the embedding on the first
+    stage (gather table) and the last (tied head), the final norm on the last."""
+    names = []
+    for name in weight_shapes(cfg):
+        if name.startswith("model.layers."):
+            if first <= int(name.split(".")[2]) < end:
+                names.append(name)
+        elif name == "model.embed_tokens.weight":
+            if first == 0 or end == cfg.layers:
+                names.append(name)
+        elif end == cfg.layers:
+            names.append(name)
+    return names
+
+
+class _CudaArray:
+    """A device buffer described by __cuda_array_interface__ (v3), so torch.as_tensor can view it without a copy."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None, "stream": None}
+
+
 class QwenEngine:
     """One device's Qwen3 engine. `weights` maps HF names to bf16 bit arrays (uint16), or is the path (or a list of
     paths) of safetensors checkpoint files holding every weight of the model once (BF16, or F32 narrowed to bf16),
-    streamed to the device by the library's reader."""
+    streamed to the device by the library's reader.
+
+    `stage=(first, end)` makes it a pipeline stage holding layers [first, end) (the reference's StagePipeline split):
+    only that stage's weights are loaded (others in `weights` are skipped), a stage after the first reads its input
+    from `residual()` and a stage before the last leaves its output there; see prefill_stage and decode."""
 
     def __init__(self, cfg: QwenConfig, weights, rope_cos: np.ndarray, rope_sin: np.ndarray, device: int = 0,
                  max_seqs: int = 64, kv_pages: int | None = None, max_tokens: int = 4096, max_batch: int = 64,
-                 max_pos: int | None = None):
+                 max_pos: int | None = None, stage: tuple | None = None):
         self.cfg = cfg
+        self.first, self.end = (0, cfg.layers) if stage is None else (int(stage[0]), int(stage[1]))
+        self.is_first, self.is_last = self.first == 0, self.end == cfg.layers
+        self.device = device
         max_pos = max_pos or cfg.max_pos
         pages_per_seq = (max_pos + 15) // 16
         kv_pages = kv_pages or max_seqs * pages_per_seq
         c = QwenConfigC(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate, cfg.vocab,
                         cfg.eps, max_pos, max_seqs, kv_pages, max_tokens, max_batch)
         h = ctypes.c_void_p()
-        N.check(N.lib().lrm_qwen_create(device, ctypes.byref(c), ctypes.byref(h)), None, "lrm_qwen_create")
+        N.check(N.lib().lrm_qwen_create_stage(device, ctypes.byref(c), self.first, self.end, ctypes.byref(h)), None,
+                "lrm_qwen_create_stage")
         self._h = h
         self.max_seqs, self.max_tokens, self.max_batch, self.max_pos = max_seqs, max_tokens, max_batch, max_pos
         try:
             if isinstance(weights, dict):
-                for name, shape in weight_shapes(cfg).items():
+                shapes = weight_shapes(cfg)
+                for name in stage_weight_names(cfg, self.first, self.end):
+                    shape = shapes[name]
                     w = np.ascontiguousarray(weights[name], np.uint16)
                     if w.shape != tuple(shape):
                         raise ValueError(f"{name} is {w.shape}, expected {shape}")
@@ -103,7 +140,8 @@ class QwenEngine:
         return int(n.value)
 
     def load_checkpoint(self, paths) -> None:
-        """Loads a checkpoint split over `paths`; every weight of the model must come exactly once."""
+        """Loads a checkpoint split over `paths`; every weight of the model must come exactly once (a stage takes
+        its own and skips the rest)."""
         from .safetensors import SafetensorsFile
 
         want = set(weight_shapes(self.cfg))
@@ -116,7 +154,8 @@ class QwenEngine:
                 raise ValueError(f"{p}: " + (f"tensors loaded twice: {sorted(dup)[:3]}" if dup else
                                              f"not weights of this model: {sorted(extra)[:3]}"))
             seen |= names
-            self.load_safetensors(p)
+            if names & set(stage_weight_names(self.cfg, self.first, self.end)):
+                self.load_safetensors(p)
         if seen != want:
             raise ValueError(f"the checkpoint misses {len(want - seen)} weights, e.g. {sorted(want - seen)[:3]}")
 
@@ -139,23 +178,51 @@ class QwenEngine:
 
     def prefill(self, slots, prompts, want_logits=False):
         """Fresh prefill of prompts[i] into slots[i]; returns (next ids [n], last-row logits [n, vocab] or None)."""
+        return self.prefill_stage(slots, [len(p) for p in prompts], prompts, want_logits)
+
+    def prefill_stage(self, slots, lens, prompts=None, want_logits=False):
+        """Fresh prefill of sequences of `lens` tokens into `slots`. The first stage takes the token ids (`prompts`);
+        a later stage reads the previous stage's residual rows (sequences packed in order) from residual(). Returns
+        (next ids, logits or None) on the last stage, (None, None) on the others."""
         slots = np.ascontiguousarray(slots, np.int32)
-        lens = np.array([len(p) for p in prompts], np.int32)
-        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]), np.uint32)
-        nxt = np.empty(len(prompts), np.uint32)
-        logits = np.empty((len(prompts), self.cfg.vocab), np.float32) if want_logits else None
-        self._check(N.lib().lrm_qwen_prefill(self._h, len(prompts), _p(slots, I32), _p(lens, I32), _p(ids, U32),
-                                             _p(nxt, U32), _p(logits, F32) if want_logits else None), "prefill")
+        lens = np.ascontiguousarray(lens, np.int32)
+        ids = None
+        if self.is_first:
+            ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]), np.uint32)
+        nxt = np.empty(len(slots), np.uint32) if self.is_last else None
+        logits = np.empty((len(slots), self.cfg.vocab), np.float32) if want_logits and self.is_last else None
+        self._check(N.lib().lrm_qwen_prefill(self._h, len(slots), _p(slots, I32), _p(lens, I32),
+                                             _p(ids, U32) if ids is not None else None,
+                                             _p(nxt, U32) if nxt is not None else None,
+                                             _p(logits, F32) if logits is not None else None), "prefill")
         return nxt, logits
 
-    def decode(self, slots, ids, want_logits=False):
+    def decode(self, slots, ids=None, want_logits=False):
+        """One decode step: ids[b] appended to slots[b] (the first stage; later stages read the residual rows).
+        Returns (next ids, logits or None) on the last stage, (None, None) on the others."""
         slots = np.ascontiguousarray(slots, np.int32)
-        ids = np.ascontiguousarray(ids, np.uint32)
-        nxt = np.empty(len(slots), np.uint32)
-        logits = np.empty((len(slots), self.cfg.vocab), np.float32) if want_logits else None
-        self._check(N.lib().lrm_qwen_decode(self._h, len(slots), _p(slots, I32), _p(ids, U32), _p(nxt, U32),
-                                            _p(logits, F32) if want_logits else None), "decode")
+        ids = np.ascontiguousarray(ids, np.uint32) if self.is_first else None
+        nxt = np.empty(len(slots), np.uint32) if self.is_last else None
+        logits = np.empty((len(slots), self.cfg.vocab), np.float32) if want_logits and self.is_last else None
+        self._check(N.lib().lrm_qwen_decode(self._h, len(slots), _p(slots, I32),
+                                            _p(ids, U32) if ids is not None else None,
+                                            _p(nxt, U32) if nxt is not None else None,
+                                            _p(logits, F32) if logits is not None else None), "decode")
         return nxt, logits
+
+    def residual(self, rows: int | None = None):
+        """The fp32 residual x [rows, hidden] as a torch tensor viewing the engine's device buffer (no copy): the
+        boundary a pipeline stage reads from and writes to. Work on it must be ordered with the engine's calls
+        (synchronise, or use the engine's stream)."""
+        import torch
+
+        ptr, cap = P(), ctypes.c_int64()
+        self._check(N.lib().lrm_qwen_residual(self._h, ctypes.byref(ptr), ctypes.byref(cap)), "residual")
+        rows = int(cap.value) if rows is None else int(rows)
+        if rows > cap.value:
+            raise ValueError(f"the residual holds {cap.value} rows")
+        with torch.cuda.device(self.device):
+            return torch.as_tensor(_CudaArray(ptr.value, (rows, self.cfg.hidden), "<f4"), device=f"cuda:{self.device}")
 
     def capture(self, slots, first_ids=None, time_attention=False):
         """Captures the device-resident decode step for `slots` (inputs: the previous step's outputs)."""
@@ -172,7 +239,7 @@ class QwenEngine:
         return v.value
 
     def attention_ms(self) -> np.ndarray:
-        out = np.empty(self.cfg.layers, np.float32)
+        out = np.empty(self.end - self.first, np.float32)
         self._check(N.lib().lrm_qwen_attention_ms(self._h, _p(out, F32)), "attention_ms")
         return out
 
