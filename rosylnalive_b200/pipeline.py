@@ -132,15 +132,26 @@ class DistPipeline:
 
     `engine` is this rank's stage. Every rank calls greedy() with the same arguments; rank 0 returns the ids, the
     others None. Tensors travel with torch.distributed point-to-point calls on the default group (NCCL for CUDA
-    engines, gloo for host ones); `device` is where the transfer buffers live. Sends are non-blocking (isend), so
-    no order of the ranks' progress can deadlock: rank 0 takes a microbatch's ids from the last rank only right
-    before it needs them for that microbatch's next step."""
+    engines, gloo for host ones); `device` is where the transfer buffers live.
+
+    No order of the ranks' progress can deadlock: sends are non-blocking (isend); rank 0 takes a microbatch's ids
+    from the last rank only right before it needs them for that microbatch's next step; and the residual rows
+    (forward) and the ids (back) travel on two process groups. One communicator runs a rank's point-to-point calls
+    in the order they were posted, so with a single group rank 0's queued residual sends would wait behind rank 1's
+    ids send, which waits for rank 0's ids receive behind those sends, once a message is too large to go eagerly.
+    Every rank constructs DistPipeline at the same point (the groups are created collectively)."""
 
     def __init__(self, engine, rank: int, world: int, device):
         self.engine, self.rank, self.world, self.device = engine, rank, world, device
         if engine.is_first != (rank == 0) or engine.is_last != (rank == world - 1):
             raise ValueError(f"rank {rank} of {world} holds layers [{engine.first}, {engine.end})")
         self._inflight = []
+        self._fwd = self._back = None
+        if world > 1:
+            import torch.distributed as dist
+
+            self._fwd = dist.new_group(list(range(world)))
+            self._back = dist.new_group(list(range(world)))
 
     def _sync(self):
         import torch
@@ -148,11 +159,11 @@ class DistPipeline:
         if str(self.device).startswith("cuda"):
             torch.cuda.synchronize(self.device)
 
-    def _isend(self, t, dst):
+    def _isend(self, t, dst, group):
         import torch.distributed as dist
 
         self._inflight = [(r, x) for r, x in self._inflight if not r.is_completed()]
-        self._inflight.append((dist.isend(t, dst), t))  # the tensor stays alive until the send completes
+        self._inflight.append((dist.isend(t, dst, group=group), t))  # the tensor stays alive until sent
 
     def _drain(self):
         for req, _ in self._inflight:
@@ -170,7 +181,7 @@ class DistPipeline:
         rows = int(np.sum(lens)) if kind == "prefill" else len(slots)
         if self.rank > 0:
             buf = torch.empty((rows, e.cfg.hidden), dtype=torch.float32, device=self.device)
-            dist.recv(buf, self.rank - 1)
+            dist.recv(buf, self.rank - 1, group=self._fwd)
             self._sync()
             e.residual(rows).copy_(buf)
             self._sync()
@@ -181,11 +192,11 @@ class DistPipeline:
         if not e.is_last:
             out = e.residual(rows).clone()
             self._sync()
-            self._isend(out, self.rank + 1)
+            self._isend(out, self.rank + 1, self._fwd)
         elif self.world > 1:
             back = torch.from_numpy(nxt.astype(np.int64)).to(self.device)
             self._sync()
-            self._isend(back, 0)
+            self._isend(back, 0, self._back)
         return nxt
 
     def _ids_back(self, n):
@@ -194,7 +205,7 @@ class DistPipeline:
         import torch.distributed as dist
 
         buf = torch.empty(n, dtype=torch.int64, device=self.device)
-        dist.recv(buf, self.world - 1)
+        dist.recv(buf, self.world - 1, group=self._back)
         return buf.cpu().numpy().astype(np.uint32)
 
     @staticmethod
