@@ -292,6 +292,12 @@ lrm_status lrm_qwen_reserve(lrm_qwen q, int32_t slot, int32_t tokens);
 lrm_status lrm_qwen_prefill(lrm_qwen q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
                             uint32_t *next_ids, float *logits);
 
+/* Chunked prefill: like lrm_qwen_prefill, but each sequence's lens[i] tokens continue the tokens slots[i] already
+ * holds (from a prefill, decode steps or earlier extends; a slot holding none starts at 0), attending to all of them.
+ * Splitting a prompt into chunks gives the same ids and logits, bit for bit, as one prefill of the whole prompt. */
+lrm_status lrm_qwen_extend(lrm_qwen q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
+                           uint32_t *next_ids, float *logits);
+
 /* One decode step: token ids[b] (host) appended to slots[b]; next greedy ids (host, [batch]) and optional logits
  * (host, [batch, vocab]). Uses the captured graph when one exists for the same slots. */
 lrm_status lrm_qwen_decode(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *ids, uint32_t *next_ids,

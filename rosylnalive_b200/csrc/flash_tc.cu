@@ -2,7 +2,10 @@
 //
 // One CTA owns 128 query rows of up to two query heads that share a KV head (two "slots"; one when the group size
 // q_heads / kv_heads is odd), so every K/V tile is loaded once for both, and walks the 128-key tiles up to the causal
-// limit. Tensor memory (512 columns) holds per slot S (128 x 128 fp32) and O (128 x 128 fp32); P overwrites S in
+// limit. K and V come either from contiguous [tokens][kv_heads][128] arrays (sequences packed, positions from 0) or
+// from the paged KV cache (a 128-key tile = 8 pages of 16 tokens, one TMA box per page and half tile), in which case
+// a sequence's rows are a chunk that continues `past` cached tokens: chunked prefill, and prefill onto a decoded
+// sequence, attend to every cached key with the same per-row arithmetic as one whole prefill. Tensor memory (512 columns) holds per slot S (128 x 128 fp32) and O (128 x 128 fp32); P overwrites S in
 // place as bf16 and the P V product reads it from tensor memory, so P never goes through shared memory.
 //   warp 0      TMA producer: Q of both slots once, then K_0, V_0, K_1, V_1, ... (3D tensor maps over
 //               [tokens][heads][128], 128-byte swizzle, boxes of 64 dims x 128 rows) through a ring of five 32 KiB
@@ -56,6 +59,9 @@ struct FlashTcParams {
     int nseq, max_len, q_heads, kv_heads, heads_per_cta;
     float scale_log2;
     uint32_t *err;
+    // paged K/V (paged != 0): page table [slots][pages_per_seq], each sequence's slot and cached tokens before it
+    const int32_t *pages, *seq_slot, *past;
+    int pages_per_seq, paged;
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -121,7 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q0 = qt * TQ;
     if (q0 >= len) return;  // whole CTA, before any barrier or TMEM use
     const int kvh = h0 / (p.q_heads / p.kv_heads);
-    const int n_kt = (min(len, q0 + TQ) - 1) / TK + 1;
+    const int past = p.paged ? p.past[seq] : 0;  // row r of the chunk is position past + r
+    const int n_kt = (past + min(len, q0 + TQ) - 1) / TK + 1;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -182,10 +189,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int st = i % KV_ST;
                     if (!ptx::mbar_wait(&kv_empty[st], ((i / KV_ST) & 1) ^ 1, err, 0x3001)) break;
                     const CUtensorMap *map = (i & 1) ? &tv : &tk;
-                    const int rows = start + (i >> 1) * TK;
                     ptx::mbar_arrive_expect_tx(&kv_full[st], TILE);
-                    ptx::tma_load_3d(sKV + st * TILE, map, &kv_full[st], 0, kvh, rows);
-                    ptx::tma_load_3d(sKV + st * TILE + SUB, map, &kv_full[st], 64, kvh, rows);
+                    if (p.paged) {
+                        // 8 pages of 16 keys; a page index past the table (keys past the sequence, masked) reads
+                        // page 0, whose values are finite and get weight 0
+                        const int32_t *prow = p.pages + (size_t)p.seq_slot[seq] * p.pages_per_seq;
+                        int pg[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int idx = (i >> 1) * 8 + u;
+                            pg[u] = idx < p.pages_per_seq ? prow[idx] : 0;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int c2 = (pg[u] * p.kv_heads + kvh) * 2 + (i & 1);
+                            ptx::tma_load_3d(sKV + st * TILE + u * 2048, map, &kv_full[st], 0, 0, c2);
+                            ptx::tma_load_3d(sKV + st * TILE + SUB + u * 2048, map, &kv_full[st], 64, 0, c2);
+                        }
+                    } else {
+                        const int rows = start + (i >> 1) * TK;
+                        ptx::tma_load_3d(sKV + st * TILE, map, &kv_full[st], 0, kvh, rows);
+                        ptx::tma_load_3d(sKV + st * TILE + SUB, map, &kv_full[st], 64, kvh, rows);
+                    }
                 }
                 // Our own copies in flight must land before the CTA exits (this matters on the error path).
                 ptx::mbar_wait(q_full, 0, err, 0x3002);
@@ -271,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int s = (warp - 4) >> 2;
             const int q = warp & 3;  // TMEM lane quarter this warp may access
             const int rl = q * 32 + lane;
-            const int row = q0 + rl;  // query position within the sequence
+            const int row = q0 + rl;  // query row within the chunk; its position is past + row
             const uint32_t lane_off = (uint32_t)(q * 32) << 16;
             const uint32_t tS = tmem + 256 * s + lane_off, tO = tS + 128;
             const float sc = p.scale_log2;
@@ -291,9 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptx::tmem_ld_wait();
                 const int key0 = j * TK;
                 // Masking is needed when some key of the tile lies past the warp's first row or past the sequence.
-                const bool need_mask = key0 + TK - 1 > q0 + q * 32 || key0 + TK > len;
+                const bool need_mask = key0 + TK - 1 > past + q0 + q * 32 || key0 + TK > past + len;
                 if (need_mask) {
-                    const int lim = min(row - key0, len - 1 - key0);  // keys 0..lim of the tile are visible
+                    const int lim = min(past + row - key0, past + len - 1 - key0);  // keys 0..lim are visible
 #pragma unroll
                     for (int e = 0; e < 128; ++e) x[e] = e <= lim ? x[e] : -INFINITY;
                 }
@@ -346,18 +371,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         pk[e] = pack2(a, b);
                     }
                 } else {
+                    // the same sums in the same order as the masked form, so a row's result does not depend on
+                    // whether its warp's tile needed a mask (chunked prefill equals whole prefill bit for bit)
 #pragma unroll
                     for (int e = 0; e < 64; ++e) {
                         float a, b;
                         fma2(a, b, x[2 * e], x[2 * e + 1], sc, sc, nm, nm);
                         if (kEmuEvery > 0 && e % kEmuEvery == kEmuEvery - 1) {
                             exp2_poly2(a, b, a, b);
-                            add2(lc, ld, lc, ld, a, b);
                         } else {
                             a = ptx::ex2(a);
                             b = ptx::ex2(b);
-                            add2(la, lb, la, lb, a, b);
                         }
+                        if (e & 1)
+                            add2(lc, ld, lc, ld, a, b);
+                        else
+                            add2(la, lb, la, lb, a, b);
                         pk[e] = pack2(a, b);
                     }
                 }
@@ -431,13 +460,34 @@ bool make_tmap_heads(CUtensorMap *map, const void *ptr, int heads, int tokens) {
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The paged KV pool [pages][kv_heads][2][16][128] bf16 as [pages * kv_heads * 2][16 tokens][128]: boxes of 64 dims x
+// 16 tokens (one page of one head, K or V), 128-byte swizzle.
+bool make_tmap_pool(CUtensorMap *map, const void *pool, int kv_heads, int pages) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {128, 16, (cuuint64_t)pages * kv_heads * 2};
+    cuuint64_t strides[2] = {256, 16 * 256};
+    cuuint32_t box[3] = {64, 16, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(pool), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_tokens, uint32_t *err, cudaStream_t st) {
     CUtensorMap tq, tk, tv;
-    if (!make_tmap_heads(&tq, a.q, a.q_heads, total_tokens) || !make_tmap_heads(&tk, a.k, a.kv_heads, total_tokens) ||
-        !make_tmap_heads(&tv, a.v, a.kv_heads, total_tokens))
+    if (!make_tmap_heads(&tq, a.q, a.q_heads, total_tokens)) return cudaErrorInvalidValue;
+    if (a.pool) {
+        if (!a.pages || !a.seq_slot || !a.past || a.pages_per_seq < 1 || a.kv_pages < 1 ||
+            !make_tmap_pool(&tk, a.pool, a.kv_heads, a.kv_pages))
+            return cudaErrorInvalidValue;
+        tv = tk;
+    } else if (!make_tmap_heads(&tk, a.k, a.kv_heads, total_tokens) ||
+               !make_tmap_heads(&tv, a.v, a.kv_heads, total_tokens)) {
         return cudaErrorInvalidValue;
+    }
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -456,6 +506,11 @@ cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_toke
     p.heads_per_cta = ((a.q_heads / a.kv_heads) % 2 == 0) ? 2 : 1;
     p.scale_log2 = a.scale_log2;
     p.err = err;
+    p.paged = a.pool != nullptr;
+    p.pages = a.pages;
+    p.seq_slot = a.seq_slot;
+    p.past = a.past;
+    p.pages_per_seq = a.pages_per_seq;
     dim3 grid(a.q_heads / p.heads_per_cta, a.nseq, (a.max_len + TQ - 1) / TQ);
     return launch_kernel(flash_tc_kernel, grid, dim3(kThreads), SMEM_BYTES, st, tq, tk, tv, p);
 }

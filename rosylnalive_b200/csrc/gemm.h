@@ -12,8 +12,9 @@ enum GemmEpi : int { EPI_F32 = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3
 
 // The q/k/v epilogue (EPI_QKV): the output columns are head rows of 128 (q heads, then k heads, then v heads); each
 // thread owns one token row of one head, applies the per-head RMSNorm (q_norm / k_norm) and NeoX RoPE to q and k at
-// the token's position, and writes bf16 q to q_out [T][q_heads][128], k and v to k_out / v_out [T][kv_heads][128]
-// and into the paged cache (pool [pages][kv_heads][2][16][128], page table [slots][pages_per_seq]).
+// the token's position, and writes bf16 q to q_out [T][q_heads][128], k and v into the paged cache (pool
+// [pages][kv_heads][2][16][128], page table [slots][pages_per_seq]) and, when k_out / v_out are not null, to
+// contiguous copies [T][kv_heads][128].
 struct QkvEpilogue {
     __nv_bfloat16 *q_out, *k_out, *v_out, *pool;
     const int32_t *pages;

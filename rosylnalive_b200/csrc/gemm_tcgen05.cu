@@ -104,7 +104,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_r
                     dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
                 } else {
                     const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
-                    dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
+                    __nv_bfloat16 *flat = is_k ? E.k_out : E.v_out;  // optional contiguous copy
+                    dst0 = flat ? flat + ((size_t)row * E.kv_heads + kvh) * 128 : nullptr;
                     const int page = E.pages[(size_t)slot * E.pages_per_seq + pos / 16];
                     dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
                            ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + pos % 16) * 128;
@@ -123,7 +124,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_r
                     a[j] = has_k ? __uint_as_float(lo[j]) : 0.f;
                     b[j] = has_k ? __uint_as_float(hi[j]) : 0.f;
                 }
-                if (rotate && dst0) {
+                if (rotate && (dst0 || dst1)) {
                     const float4 *cs4 = reinterpret_cast<const float4 *>(E.cos_t + (size_t)pos * 64 + 16 * c);
                     const float4 *sn4 = reinterpret_cast<const float4 *>(E.sin_t + (size_t)pos * 64 + 16 * c);
                     const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
@@ -154,7 +155,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_r
                         b[j] = x1 * cf[j] + x0 * sf[j];
                     }
                 }
-                if (dst0) {
+                if (dst0 || dst1) {
                     uint32_t pl[8], ph[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -163,9 +164,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_r
                     }
                     const uint4 l0 = make_uint4(pl[0], pl[1], pl[2], pl[3]), l1 = make_uint4(pl[4], pl[5], pl[6], pl[7]);
                     const uint4 h0 = make_uint4(ph[0], ph[1], ph[2], ph[3]), h1 = make_uint4(ph[4], ph[5], ph[6], ph[7]);
-                    uint4 *d0 = reinterpret_cast<uint4 *>(dst0 + 16 * c);
-                    uint4 *e0 = reinterpret_cast<uint4 *>(dst0 + 64 + 16 * c);
-                    d0[0] = l0; d0[1] = l1; e0[0] = h0; e0[1] = h1;
+                    if (dst0) {
+                        uint4 *d0 = reinterpret_cast<uint4 *>(dst0 + 16 * c);
+                        uint4 *e0 = reinterpret_cast<uint4 *>(dst0 + 64 + 16 * c);
+                        d0[0] = l0; d0[1] = l1; e0[0] = h0; e0[1] = h1;
+                    }
                     if (dst1) {
                         uint4 *d1 = reinterpret_cast<uint4 *>(dst1 + 16 * c);
                         uint4 *e1 = reinterpret_cast<uint4 *>(dst1 + 64 + 16 * c);
@@ -654,7 +657,8 @@ __device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32
                 dst0 = E.q_out + ((size_t)row * E.q_heads + head_row) * 128;
             } else {
                 const int kvh = is_k ? head_row - E.q_heads : head_row - E.q_heads - E.kv_heads;
-                dst0 = (is_k ? E.k_out : E.v_out) + ((size_t)row * E.kv_heads + kvh) * 128;
+                __nv_bfloat16 *flat = is_k ? E.k_out : E.v_out;  // optional contiguous copy
+                dst0 = flat ? flat + ((size_t)row * E.kv_heads + kvh) * 128 : nullptr;
                 const int page = E.pages[(size_t)R.slot * E.pages_per_seq + R.pos / 16];
                 dst1 = E.pool + (size_t)page * E.kv_heads * 2 * 16 * 128 +
                        ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + R.pos % 16) * 128;
@@ -996,8 +1000,8 @@ const char *gemm_check(const GemmArgs &a) {
         const QkvEpilogue &q = a.qkv;
         if (a.bn < 128 || a.N % 128 || a.N != (q.q_heads + 2 * q.kv_heads) * 128)
             return "the q/k/v epilogue needs bn >= 128 and N = (q_heads + 2 kv_heads) * 128";
-        if (!q.q_out || !q.k_out || !q.v_out || !q.pool || !q.pages || !q.q_norm || !q.k_norm || !q.cos_t ||
-            !q.sin_t || !q.tok_slot || !q.tok_pos)
+        if (!q.q_out || !q.pool || !q.pages || !q.q_norm || !q.k_norm || !q.cos_t || !q.sin_t || !q.tok_slot ||
+            !q.tok_pos)
             return "the q/k/v epilogue is missing a pointer";
         if (((uintptr_t)q.q_out | (uintptr_t)q.k_out | (uintptr_t)q.v_out | (uintptr_t)q.pool) & 15)
             return "the q/k/v epilogue outputs must be 16-byte aligned";

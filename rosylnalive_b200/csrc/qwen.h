@@ -72,14 +72,19 @@ struct DecodeAttnArgs {
 };
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st);
 
-// Causal prefill attention over contiguous q [T][q_heads][128], k/v [T][kv_heads][128] for sequences packed by
-// cu_seqlens (positions start at 0 in each); out bf16 [T][q_heads][128].
+// Causal prefill attention for query rows q [T][q_heads][128] of sequences packed by cu_seqlens; out bf16
+// [T][q_heads][128]. K/V either contiguous (k/v [T][kv_heads][128], positions from 0 in each sequence; pool null) or
+// paged (pool non-null: sequence i's rows continue past[i] cached tokens of slot seq_slot[i], and its keys
+// 0 .. past[i] + rows - 1 are read from the cache, where the rows' own k/v must already be).
 struct PrefillAttnArgs {
-    const __nv_bfloat16 *q, *k, *v;
+    const __nv_bfloat16 *q, *k = nullptr, *v = nullptr;
     __nv_bfloat16 *out;
     const int32_t *cu_seqlens;  // [nseq + 1]
     int nseq, max_len, q_heads, kv_heads;
     float scale_log2;
+    const __nv_bfloat16 *pool = nullptr;  // this layer's pool [kv_pages][kv_heads][2][16][128]
+    const int32_t *pages = nullptr, *seq_slot = nullptr, *past = nullptr;
+    int pages_per_seq = 0, kv_pages = 0;
 };
 // Runs on tcgen05 tensor cores (TMA tiles, TMEM accumulators); total_tokens = rows of q/k/v.
 cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_tokens, uint32_t *err, cudaStream_t st);

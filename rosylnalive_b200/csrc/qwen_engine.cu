@@ -8,8 +8,8 @@
 //   embed_norm                                        advance (positions, lengths) ; embed_norm
 //   per layer:                                        per layer:
 //     GEMM xn.Wqkv^T -> qkv fp32                        GEMM Wqkv.xn^T split-K -> partials
-//     qk_norm_rope_kv -> q, k, v (+ paged cache)        qk_norm_rope_kv (reduces the splits)
-//     flash prefill attention -> attn                   paged split-K decode attention + combine
+//     (q/k/v epilogue: q; k, v into the paged cache)    qk_norm_rope_kv (reduces the splits)
+//     flash prefill attention over the cache -> attn    paged split-K decode attention + combine
 //     GEMM attn.Wo^T, epilogue x += .                   GEMM Wo.attn^T split-K ; resid_norm (x += sum; norm)
 //     resid_norm (post norm) -> xn                      GEMM Wgu.xn^T split-K ; swiglu_reduce
 //     GEMM xn.Wgu^T, SwiGLU epilogue -> act             GEMM Wdown.act^T split-K ; resid_norm (next norm)
@@ -91,9 +91,9 @@ struct lrm_qwen_s {
     uint8_t *amem = nullptr;
     uint32_t *ids = nullptr, *next = nullptr;
     int32_t *tok_slot = nullptr, *tok_pos = nullptr, *cu = nullptr, *last_idx = nullptr, *d_slots = nullptr;
+    int32_t *pf_slot = nullptr, *pf_past = nullptr;  // per prefill sequence: its slot and cached tokens before it
     float *x = nullptr, *qkv = nullptr, *partial = nullptr, *part_o = nullptr, *part_ml = nullptr;
-    __nv_bfloat16 *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
-                  *xl = nullptr;
+    __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xl = nullptr;
     size_t partial_elems = 0;
     int max_splits_attn = 0;
     int pps = 32;
@@ -377,10 +377,10 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     if (dec > part) part = dec;
     Q->partial_elems = part;
     size_t abytes = 0;
-    abytes += (size_t)T * 4 * 3 + (size_t)R * 4 * 3 + (size_t)(c.max_seqs + 1) * 4 * 2;
+    abytes += (size_t)T * 4 * 3 + (size_t)R * 4 * 3 + (size_t)(c.max_seqs + 1) * 4 * 4;
     abytes += (size_t)T * H * 4 + (size_t)T * Q->qkv_rows * 4 + part * 4;
     abytes += (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * (128 + 2) * 4;
-    abytes += (size_t)T * (H + qh * kHeadDim * 2 + 2 * kvh * kHeadDim + I) * 2 + (size_t)R * H * 2;
+    abytes += (size_t)T * (H + qh * kHeadDim * 2 + I) * 2 + (size_t)R * H * 2;
     abytes += 64 * 256;
     QTRY(Q.get(), cudaMalloc(&Q->amem, abytes), "activations");
     p = Q->amem;
@@ -391,6 +391,8 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     Q->last_idx = carve<int32_t>(p, R);
     Q->d_slots = carve<int32_t>(p, R);
     Q->cu = carve<int32_t>(p, c.max_seqs + 1);
+    Q->pf_slot = carve<int32_t>(p, c.max_seqs);
+    Q->pf_past = carve<int32_t>(p, c.max_seqs);
     Q->x = carve<float>(p, (size_t)T * H);
     Q->qkv = carve<float>(p, (size_t)T * Q->qkv_rows);
     Q->partial = carve<float>(p, part);
@@ -398,8 +400,6 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     Q->part_ml = carve<float>(p, (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * 2);
     Q->xn = carve<__nv_bfloat16>(p, (size_t)T * H);
     Q->q = carve<__nv_bfloat16>(p, (size_t)T * qh * kHeadDim);
-    Q->k = carve<__nv_bfloat16>(p, (size_t)T * kvh * kHeadDim);
-    Q->v = carve<__nv_bfloat16>(p, (size_t)T * kvh * kHeadDim);
     Q->attn = carve<__nv_bfloat16>(p, (size_t)T * qh * kHeadDim);
     Q->act = carve<__nv_bfloat16>(p, (size_t)T * I);
     Q->xl = carve<__nv_bfloat16>(p, (size_t)R * H);
@@ -628,44 +628,55 @@ lrm_status lrm_qwen_reserve(lrm_qwen Q, int32_t slot, int32_t tokens) {
     return changed ? upload_page_row(Q, slot) : LRM_OK;
 }
 
-lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
-                            uint32_t *next_ids, float *logits) {
+// Prefill of `nseq` sequences packed together. Fresh (extend false): each slot is reset first. Extend: each
+// sequence's rows continue the tokens its slot already holds (chunked prefill), attending to all of them.
+static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, const int32_t *lens,
+                              const uint32_t *ids, uint32_t *next_ids, float *logits, bool extend) {
     LTRY(check_ready(Q));
     const lrm_qwen_config &c = Q->c;
     if (nseq < 1 || nseq > c.max_seqs || !slots || !lens || (Q->is_first && !ids) || (Q->is_last && !next_ids))
         return qfail(Q, LRM_ERR_ARGUMENT, "bad prefill arguments");
-    std::vector<int32_t> cu(nseq + 1, 0), last(nseq), tslot, tpos;
+    std::vector<int32_t> cu(nseq + 1, 0), last(nseq), past(nseq, 0), tslot, tpos;
     int max_len = 0;
     for (int i = 0; i < nseq; ++i) {
-        if (lens[i] < 1 || lens[i] > c.max_pos || slots[i] < 0 || slots[i] >= c.max_seqs)
-            return qfail(Q, LRM_ERR_ARGUMENT, "bad sequence length or slot");
+        if (slots[i] < 0 || slots[i] >= c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "bad sequence slot");
+        for (int i2 = 0; i2 < i; ++i2)
+            if (slots[i2] == slots[i]) return qfail(Q, LRM_ERR_ARGUMENT, "a slot appears twice in one prefill");
+        past[i] = extend ? Q->h_seq_len[slots[i]] : 0;
+        if (lens[i] < 1 || past[i] + lens[i] > c.max_pos)
+            return qfail(Q, LRM_ERR_ARGUMENT, "bad sequence length (rows of a call >= 1, cached + rows <= max_pos)");
         cu[i + 1] = cu[i] + lens[i];
         last[i] = cu[i + 1] - 1;
         if (lens[i] > max_len) max_len = lens[i];
     }
     const int T = cu[nseq];
     if (T > c.max_tokens) return qfail(Q, LRM_ERR_ARGUMENT, "more tokens than max_tokens");
-    for (int i = 0; i < nseq; ++i) {
-        if (uint32_t(slots[i]) >= (uint32_t)c.max_seqs) return LRM_ERR_ARGUMENT;
-        LTRY(lrm_qwen_reset_seq(Q, slots[i]));
-        LTRY(lrm_qwen_reserve(Q, slots[i], lens[i]));
-        for (int t = 0; t < lens[i]; ++t) {
-            tslot.push_back(slots[i]);
-            tpos.push_back(t);
-        }
-        Q->h_seq_len[slots[i]] = lens[i];
-    }
     if (Q->is_first)
         for (int i = 0; i < T; ++i)
             if (ids[i] >= (uint32_t)c.vocab) return qfail(Q, LRM_ERR_ARGUMENT, "an id is outside the vocabulary");
+    for (int i = 0; i < nseq; ++i) {
+        if (!extend) LTRY(lrm_qwen_reset_seq(Q, slots[i]));
+        LTRY(lrm_qwen_reserve(Q, slots[i], past[i] + lens[i]));
+    }
+    for (int i = 0; i < nseq; ++i) {
+        for (int t = 0; t < lens[i]; ++t) {
+            tslot.push_back(slots[i]);
+            tpos.push_back(past[i] + t);
+        }
+        Q->h_seq_len[slots[i]] = past[i] + lens[i];
+    }
+    std::vector<int32_t> new_len(nseq);
+    for (int i = 0; i < nseq; ++i) new_len[i] = past[i] + lens[i];
     cudaStream_t st = Q->stream;
     if (Q->is_first) QTRY(Q, cudaMemcpyAsync(Q->ids, ids, 4 * (size_t)T, cudaMemcpyHostToDevice, st), "ids");
     QTRY(Q, cudaMemcpyAsync(Q->tok_slot, tslot.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "slots");
     QTRY(Q, cudaMemcpyAsync(Q->tok_pos, tpos.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "positions");
     QTRY(Q, cudaMemcpyAsync(Q->cu, cu.data(), 4 * (size_t)(nseq + 1), cudaMemcpyHostToDevice, st), "cu_seqlens");
     QTRY(Q, cudaMemcpyAsync(Q->last_idx, last.data(), 4 * (size_t)nseq, cudaMemcpyHostToDevice, st), "last rows");
+    QTRY(Q, cudaMemcpyAsync(Q->pf_slot, slots, 4 * (size_t)nseq, cudaMemcpyHostToDevice, st), "slots");
+    QTRY(Q, cudaMemcpyAsync(Q->pf_past, past.data(), 4 * (size_t)nseq, cudaMemcpyHostToDevice, st), "past");
     for (int i = 0; i < nseq; ++i)
-        QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slots[i], &lens[i], 4, cudaMemcpyHostToDevice, st), "seq_len");
+        QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slots[i], &new_len[i], 4, cudaMemcpyHostToDevice, st), "seq_len");
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
     PdlScope pdl;
     if (Q->is_first)
@@ -678,8 +689,8 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         // q/k/v GEMM with QK-RMSNorm, RoPE and the paged KV append in its epilogue (no fp32 q/k/v round trip).
         QkvEpilogue qe;
         qe.q_out = Q->q;
-        qe.k_out = Q->k;
-        qe.v_out = Q->v;
+        qe.k_out = nullptr;  // attention reads k and v from the cache
+        qe.v_out = nullptr;
         qe.pool = Q->pool + (size_t)l * Q->layer_pool_elems;
         qe.pages = Q->d_pages;
         qe.pages_per_seq = Q->maxp;
@@ -695,8 +706,6 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         LTRY(gemm(Q, Q->xn, L.w_qkv, T, Q->qkv_rows, H, EPI_QKV, 256, 1, nullptr, Q->qkv_rows, nullptr, 0, 0, &qe));
         PrefillAttnArgs pa;
         pa.q = Q->q;
-        pa.k = Q->k;
-        pa.v = Q->v;
         pa.out = Q->attn;
         pa.cu_seqlens = Q->cu;
         pa.nseq = nseq;
@@ -704,6 +713,12 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
         pa.q_heads = qh;
         pa.kv_heads = kvh;
         pa.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+        pa.pool = qe.pool;
+        pa.pages = Q->d_pages;
+        pa.seq_slot = Q->pf_slot;
+        pa.past = Q->pf_past;
+        pa.pages_per_seq = Q->maxp;
+        pa.kv_pages = c.kv_pages;
         KTRY(Q, launch_prefill_attention_tc(pa, T, Q->err, st), "prefill_attention");
         LTRY(gemm(Q, Q->attn, L.w_o, T, H, qh * kHeadDim, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
         KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, L.post_norm, c.eps, Q->xn, st), "resid_norm");
@@ -721,6 +736,16 @@ lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, cons
     if (logits)
         QTRY(Q, cudaMemcpyAsync(logits, Q->partial, 4 * (size_t)nseq * c.vocab, cudaMemcpyDeviceToHost, st), "logits");
     return sync_check(Q);
+}
+
+lrm_status lrm_qwen_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
+                            uint32_t *next_ids, float *logits) {
+    return run_prefill(Q, nseq, slots, lens, ids, next_ids, logits, false);
+}
+
+lrm_status lrm_qwen_extend(lrm_qwen Q, int32_t nseq, const int32_t *slots, const int32_t *lens, const uint32_t *ids,
+                           uint32_t *next_ids, float *logits) {
+    return run_prefill(Q, nseq, slots, lens, ids, next_ids, logits, true);
 }
 
 static lrm_status set_slots(lrm_qwen Q, int32_t batch, const int32_t *slots) {

@@ -37,6 +37,7 @@ N.extra_signatures({
     "lrm_qwen_reset_seq": [P, I32],
     "lrm_qwen_reserve": [P, I32, I32],
     "lrm_qwen_prefill": [P, I32, PI32, PI32, PU32, PU32, PF32],
+    "lrm_qwen_extend": [P, I32, PI32, PI32, PU32, PU32, PF32],
     "lrm_qwen_decode": [P, I32, PI32, PU32, PU32, PF32],
     "lrm_qwen_decode_graph": [P, I32, PI32, PU32, U32],
     "lrm_qwen_graph_kernels": [P, PI32],
@@ -180,10 +181,16 @@ class QwenEngine:
         """Fresh prefill of prompts[i] into slots[i]; returns (next ids [n], last-row logits [n, vocab] or None)."""
         return self.prefill_stage(slots, [len(p) for p in prompts], prompts, want_logits)
 
-    def prefill_stage(self, slots, lens, prompts=None, want_logits=False):
-        """Fresh prefill of sequences of `lens` tokens into `slots`. The first stage takes the token ids (`prompts`);
-        a later stage reads the previous stage's residual rows (sequences packed in order) from residual(). Returns
-        (next ids, logits or None) on the last stage, (None, None) on the others."""
+    def extend(self, slots, chunks, want_logits=False):
+        """Chunked prefill: chunks[i] (token ids) continue the tokens slots[i] already holds, attending to all of
+        them; returns (next ids [n], last-row logits [n, vocab] or None). Prefill of a prompt's first chunk followed
+        by extend of the rest equals one prefill of the whole prompt bit for bit."""
+        return self.prefill_stage(slots, [len(c) for c in chunks], chunks, want_logits, extend=True)
+
+    def prefill_stage(self, slots, lens, prompts=None, want_logits=False, extend=False):
+        """Fresh prefill (or, with extend, a continuation) of sequences of `lens` tokens in `slots`. The first stage
+        takes the token ids (`prompts`); a later stage reads the previous stage's residual rows (sequences packed in
+        order) from residual(). Returns (next ids, logits or None) on the last stage, (None, None) on the others."""
         slots = np.ascontiguousarray(slots, np.int32)
         lens = np.ascontiguousarray(lens, np.int32)
         ids = None
@@ -191,10 +198,11 @@ class QwenEngine:
             ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]), np.uint32)
         nxt = np.empty(len(slots), np.uint32) if self.is_last else None
         logits = np.empty((len(slots), self.cfg.vocab), np.float32) if want_logits and self.is_last else None
-        self._check(N.lib().lrm_qwen_prefill(self._h, len(slots), _p(slots, I32), _p(lens, I32),
-                                             _p(ids, U32) if ids is not None else None,
-                                             _p(nxt, U32) if nxt is not None else None,
-                                             _p(logits, F32) if logits is not None else None), "prefill")
+        fn = N.lib().lrm_qwen_extend if extend else N.lib().lrm_qwen_prefill
+        self._check(fn(self._h, len(slots), _p(slots, I32), _p(lens, I32),
+                       _p(ids, U32) if ids is not None else None,
+                       _p(nxt, U32) if nxt is not None else None,
+                       _p(logits, F32) if logits is not None else None), "extend" if extend else "prefill")
         return nxt, logits
 
     def decode(self, slots, ids=None, want_logits=False):
