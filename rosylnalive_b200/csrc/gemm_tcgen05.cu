@@ -58,6 +58,22 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// The per-head RMSNorm and NeoX rotation of one dim pair (i, i + 64) of q or k, as the same operations in the same
+// order on every path (the one-CTA and CTA-pair epilogues must agree bit for bit): x = (v * r) * w, then
+// lo' = fma(x_lo, c, -(x_hi * s)) and hi' = fma(x_hi, c, x_lo * s), both lanes at once on the packed f32x2 pipe.
+__device__ __forceinline__ void norm_rope_pair(float &lo, float &hi, float r, float wl, float wh, float c, float s) {
+    asm("{\n\t.reg .b64 v, rr, w, x, xs, ns, cc, u, d;\n\t"
+        "mov.b64 v, {%0, %1};\n\tmov.b64 rr, {%2, %2};\n\tmov.b64 w, {%3, %4};\n\t"
+        "mul.rn.f32x2 x, v, rr;\n\tmul.rn.f32x2 x, x, w;\n\t"  // (x_lo, x_hi)
+        "{\n\t.reg .f32 xl, xh, nsv;\n\tmov.b64 {xl, xh}, x;\n\tmov.b64 xs, {xh, xl};\n\t"
+        "neg.f32 nsv, %6;\n\tmov.b64 ns, {nsv, %6};\n\t}\n\t"
+        "mul.rn.f32x2 u, xs, ns;\n\t"                              // (-(x_hi s), x_lo s)
+        "mov.b64 cc, {%5, %5};\n\tfma.rn.f32x2 d, x, cc, u;\n\t"
+        "mov.b64 {%0, %1}, d;\n\t}"
+        : "+f"(lo), "+f"(hi)
+        : "f"(r), "f"(wl), "f"(wh), "f"(c), "f"(s));
+}
+
 // silu(g) = g / (1 + e^-g) with the approximate division (rcp.approx, about 2 ulp in fp32; the result is rounded to
 // bf16 next), the form the decode path's swiglu_reduce uses too.
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
@@ -149,11 +165,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t t_r
                         }
                     }
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float x0 = a[j] * r * wl[j], x1 = b[j] * r * wh[j];
-                        a[j] = x0 * cf[j] - x1 * sf[j];
-                        b[j] = x1 * cf[j] + x0 * sf[j];
-                    }
+                    for (int j = 0; j < 16; ++j) norm_rope_pair(a[j], b[j], r, wl[j], wh[j], cf[j], sf[j]);
                 }
                 if (dst0 || dst1) {
                     uint32_t pl[8], ph[8];
@@ -464,7 +476,16 @@ constexpr int kPairStages = 6;
 constexpr int kPairStageBytes = 2 * 128 * BK * 2;  // A half + B half
 constexpr int kStageBuf = 32 * 128;                 // one warp's 32 rows x 128 bytes
 constexpr int kEpiBytes = 4 * 2 * kStageBuf;        // four epilogue warps, two buffers each
-constexpr int kPairSmem = kPairStages * kPairStageBytes + kEpiBytes + 1024 + 256;
+constexpr int kNormBytes = 2 * 128 * 2;           // q_norm and k_norm gains (EPI_QKV), staged once per CTA
+constexpr int kPairSmem = kPairStages * kPairStageBytes + kEpiBytes + 1024 + 256 + kNormBytes;
+// The i-th tile of a pair (tiles n fastest within a 256-row block): runs of RUN consecutive tiles, run p, p + npairs,
+// ... for pair p. The q/k/v epilogue takes 4-tile runs: a run's tiles share their rows, so the rows' RoPE table
+// entries, loaded for its first tile, serve the rest (4-tile runs keep the pairs' loads within one tile of even at
+// the prefill sizes). The other epilogues take single tiles, which keep fewer row blocks (A panels) in L2 at once.
+template <int RUN>
+__device__ __forceinline__ int pair_tile(int pair, int npairs, int i) {
+    return ((i / RUN) * npairs + pair) * RUN + i % RUN;
+}
 
 __device__ __forceinline__ uint32_t swz(uint32_t buf, int r, int chunk) {
     return buf + r * 128 + ((chunk ^ (r & 7)) << 4);
@@ -629,7 +650,7 @@ __device__ __forceinline__ void qkv_preload(const GemmArgs &args, int row, bool 
 // 0..63, 64..127); the warp then writes each row's 256 bytes to its contiguous buffer and, for k and v, to the row's
 // page of the KV cache.
 __device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32_t t_warp, int n0, uint32_t buf,
-                                                    int lane, int row, const QkvRow &R) {
+                                                    uint32_t norm_smem, int lane, int row, const QkvRow &R) {
     const QkvEpilogue &E = args.qkv;
 #pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
@@ -664,7 +685,7 @@ __device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32
                        ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * 16 + R.pos % 16) * 128;
             }
         }
-        const __nv_bfloat16 *nw = is_q ? E.q_norm : E.k_norm;
+        const uint32_t nwb = norm_smem + (is_q ? 0 : 256);  // the head's gains (q_norm or k_norm) in shared memory
 #pragma unroll
         for (int c = 0; c < 4; ++c) {  // dims 16c..16c+15 pair with 64+16c..64+16c+15
             uint32_t lo[16], hi[16];
@@ -678,21 +699,16 @@ __device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32
                 bb[j] = __uint_as_float(hi[j]);
             }
             if (rotate && R.ok) {
-                const uint4 *wl4 = reinterpret_cast<const uint4 *>(nw + 16 * c);
-                const uint4 *wh4 = reinterpret_cast<const uint4 *>(nw + 64 + 16 * c);
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
-                    const uint4 l = wl4[q], h = wh4[q];
+                    const uint4 l = ptx::ld_shared_v4(nwb + 32 * c + 16 * q), h = ptx::ld_shared_v4(nwb + 128 + 32 * c + 16 * q);
                     const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const int j = 8 * q + e;
                         const float wl = __uint_as_float((e & 1) ? (lw[e >> 1] & 0xFFFF0000u) : (lw[e >> 1] << 16));
                         const float wh = __uint_as_float((e & 1) ? (hw[e >> 1] & 0xFFFF0000u) : (hw[e >> 1] << 16));
-                        const float x0 = a[j] * r * wl, x1 = bb[j] * r * wh;
-                        const float cf = R.cs[16 * c + j], sf = R.sn[16 * c + j];
-                        a[j] = x0 * cf - x1 * sf;
-                        bb[j] = x1 * cf + x0 * sf;
+                        norm_rope_pair(a[j], bb[j], r, wl, wh, R.cs[16 * c + j], R.sn[16 * c + j]);
                     }
                 }
             }
@@ -728,6 +744,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      GemmArgs args) {
     constexpr int S = kPairStages, HALF = 128 * BK * 2;
+    constexpr int RUN = EPI == EPI_QKV ? 4 : 1;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *epi_bufs = smem + S * kPairStageBytes;
@@ -737,6 +754,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *mma_done = acc_empty + 2;
     uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
+    uint8_t *norm_gains = epi_bufs + kEpiBytes + 256;  // EPI_QKV: q_norm then k_norm, bf16
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t rank = ptx::cluster_ctarank();
@@ -778,8 +796,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bool ok = true;
             int pre = 0;
             const int row_a = (int)rank * 128, row_b = (int)rank * 128;
-            if (args.independent && pair < total) {
-                const int mb = pair / n_tiles, nb = pair % n_tiles;
+            const int t0 = pair_tile<RUN>(pair, npairs, 0);
+            if (args.independent && t0 < total) {
+                const int mb = t0 / n_tiles, nb = t0 % n_tiles;
                 pre = min(S, nkb);
                 for (int j = 0; j < pre; ++j) {
                     uint8_t *sa = smem + j * kPairStageBytes;
@@ -792,7 +811,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
             ptx::griddep_wait();
-            for (int t = pair; t < total && ok; t += npairs) {
+            for (int i = 0; ok; ++i) {
+                const int t = pair_tile<RUN>(pair, npairs, i);
+                if (t >= total) break;
                 const int mb = t / n_tiles, nb = t % n_tiles;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % S;
@@ -828,7 +849,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = ptx::idesc_bf16_f32(256, 256);
             uint32_t it = 0, local = 0;
             bool ok = true;
-            for (int t = pair; t < total && ok; t += npairs, ++local) {
+            for (int i = 0; ok; ++i, ++local) {
+                if (pair_tile<RUN>(pair, npairs, i) >= total) break;
                 const int a = local & 1;
                 if (!ptx::mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1, err, 0x1013)) break;
                 ptx::tc_fence_after();
@@ -859,7 +881,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t local = 0;
         const uint32_t rel0 = ptx::mapa(&acc_empty[0], 0), rel1 = ptx::mapa(&acc_empty[1], 0);
         const uint32_t buf = ptx::smem_u32(epi_bufs + (warp - 2) * 2 * kStageBuf);
-        for (int t = pair; t < total; t += npairs, ++local) {
+        if constexpr (EPI == EPI_QKV) {
+            if (warp == 2) {  // stage the gains once; the four epilogue warps meet on named barrier 1
+                const uint4 *src = reinterpret_cast<const uint4 *>(lane < 16 ? args.qkv.q_norm : args.qkv.k_norm);
+                reinterpret_cast<uint4 *>(norm_gains)[lane] = src[lane & 15];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        QkvRow R;
+        int r_mb = -1;
+        bool r_table = false;
+        for (int i = 0;; ++i, ++local) {
+            const int t = pair_tile<RUN>(pair, npairs, i);
+            if (t >= total) break;
             const int mb = t / n_tiles, nb = t % n_tiles;
             const int a = local & 1;
             const int row0 = mb * 256 + (int)rank * 128 + q * 32;
@@ -868,12 +902,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (bytes) ptx::prefetch_l2_bulk(args.resid + (size_t)(row0 + lane) * args.ldr + nb * 256, bytes);
             }
             if constexpr (EPI == EPI_QKV) {
-                QkvRow R;
-                qkv_preload(args, row0 + lane, nb * 256 < (args.qkv.q_heads + args.qkv.kv_heads) * 128, R);
+                // a row's position, slot and RoPE entries carry over while the run stays on the same rows
+                const bool rotates = nb * 256 < (args.qkv.q_heads + args.qkv.kv_heads) * 128;
+                if (mb != r_mb || (rotates && !r_table)) {
+                    qkv_preload(args, row0 + lane, rotates, R);
+                    r_mb = mb;
+                    r_table = rotates;
+                }
                 if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
                 ptx::tc_fence_after();
                 const uint32_t t_warp = tmem_base + a * 256 + ((uint32_t)(q * 32) << 16);
-                epilogue_qkv_staged(args, t_warp, nb * 256, buf, lane, row0 + lane, R);
+                epilogue_qkv_staged(args, t_warp, nb * 256, buf, ptx::smem_u32(norm_gains), lane, row0 + lane, R);
             } else {
                 if (!ptx::mbar_wait(&acc_full[a], (local >> 1) & 1, err, 0x1016)) break;
                 ptx::tc_fence_after();
