@@ -66,14 +66,33 @@ def weight_shapes(c: QwenConfig) -> dict:
     return s
 
 
+def tap_shapes(c: QwenConfig, T: int) -> dict:
+    """The forward's taps (the reference's tap names, goldens/tiny/g1 fwd_f32.*): name -> [rows, cols] for T rows."""
+    q, kv, H, I = c.heads * c.head_dim, c.kv_heads * c.head_dim, c.hidden, c.intermediate
+    per = {"input_layernorm.out": H, "attn.q_proj.out": q, "attn.k_proj.out": kv, "attn.v_proj.out": kv,
+           "attn.q_norm.out": q, "attn.k_norm.out": kv, "attn.q_rope": q, "attn.k_rope": kv, "attn.v_cache": kv,
+           "attn.o_proj.in": q, "attn.o_proj.out": H, "resid_mid": H, "post_attention_layernorm.out": H,
+           "mlp.gate.out": I, "mlp.up.out": I, "mlp.down.in": I, "mlp.down.out": H, "out": H}
+    s = {"embed.out": (T, H)}
+    for i in range(c.layers):
+        for k, cols in per.items():
+            s[f"L{i}.{k}"] = (T, cols)
+    s["final_norm.out"] = (T, H)
+    s["logits"] = (T, c.vocab)
+    return s
+
+
 class Fp32Executor:
     """Plans, uploads and runs the fp32 Qwen3 forward on one backend.
 
     max_tokens bounds the rows of one forward (the longest prefill chunk); the KV cache holds max_pos positions.
+    With taps, the plan adds a Taps arena (the reference's GpuExecutor plan: "taps copied into the Taps arena at
+    record time") holding every intermediate of the forward under the reference's tap names: each is copied there by
+    the command list right after the dispatch that produces it, before a later one overwrites its activation buffer.
     """
 
     def __init__(self, backend, config: QwenConfig, weights: dict, rope_cos: np.ndarray, rope_sin: np.ndarray,
-                 max_tokens: int, page_bytes: int = G.MAX_PAGE_BYTES):
+                 max_tokens: int, page_bytes: int = G.MAX_PAGE_BYTES, taps: bool = False):
         self.b = backend
         self.c = c = config
         self.max_tokens = T = max_tokens
@@ -101,6 +120,9 @@ class Fp32Executor:
             specs.append((name, G.ArenaKind.ACTIVATIONS, dt, dims, G.TensorFlags.NONE))
         specs.append(("logits", G.ArenaKind.LOGITS, f32, [T, c.vocab], G.TensorFlags.NONE))
         specs.append(("next", G.ArenaKind.LOGITS, u32, [T], G.TensorFlags.NONE))
+        self.taps = tap_shapes(c, T) if taps else {}
+        for name, dims in self.taps.items():
+            specs.append(("tap:" + name, G.ArenaKind.TAPS, f32, list(dims), G.TensorFlags.NONE))
         placements = []
         for name, arena, dt, dims, flags in specs:
             n = 1
@@ -153,56 +175,91 @@ class Fp32Executor:
 
     # -- recording ------------------------------------------------------------------------------------------------
 
+    def _tap(self, cl, name: str, src: str, rows: int):
+        """Copies rows [0, rows) of activation `src` to the Taps arena's tensor `name` (after a barrier, so the
+        dispatch that wrote it has finished)."""
+        if name not in self.taps:
+            return
+        cl.barrier()
+        cols = self.taps[name][1]
+        (ss, so), (ds, do) = self.place[src], self.place["tap:" + name]
+        cl.copy(G.BufferRange(ss, so, rows * cols * 4), G.BufferRange(ds, do, rows * cols * 4))
+
     def record_forward(self, cl, T: int, pos0: int, logits_rows: str):
         c, t = self.c, self.tok
         q, kv, H, I = c.heads * c.head_dim, c.kv_heads * c.head_dim, c.hidden, c.intermediate
         d = cl.dispatch_named
+        tap = lambda name, src: self._tap(cl, name, src, T)  # noqa: E731
         d("embed_gather_bf16", ids=t["ids"], table=t["model.embed_tokens.weight"], y=t["x"], rows=T, cols=H,
           vocab=c.vocab)
+        tap("embed.out", "x")
         for i in range(c.layers):
-            p = f"model.layers.{i}."
+            p, L = f"model.layers.{i}.", f"L{i}."
             cl.barrier()
             d("rmsnorm_rows", x=t["x"], w=t[p + HF["input_layernorm"]], y=t["h"], rows=T, cols=H, eps=self.eps)
+            tap(L + "input_layernorm.out", "h")
             cl.barrier()
             d("matmul_bf16w", x=t["h"], w=t[p + HF["q_proj"]], y=t["q"], m=T, n=q, k=H)
             d("matmul_bf16w", x=t["h"], w=t[p + HF["k_proj"]], y=t["k"], m=T, n=kv, k=H)
             d("matmul_bf16w", x=t["h"], w=t[p + HF["v_proj"]], y=t["v"], m=T, n=kv, k=H)
+            tap(L + "attn.q_proj.out", "q")
+            tap(L + "attn.k_proj.out", "k")
+            tap(L + "attn.v_proj.out", "v")
             cl.barrier()
             d("rmsnorm_rows", x=t["q"], w=t[p + HF["q_norm"]], y=t["qn"], rows=T * c.heads, cols=c.head_dim,
               eps=self.eps)
             d("rmsnorm_rows", x=t["k"], w=t[p + HF["k_norm"]], y=t["kn"], rows=T * c.kv_heads, cols=c.head_dim,
               eps=self.eps)
+            tap(L + "attn.q_norm.out", "qn")
+            tap(L + "attn.k_norm.out", "kn")
             cl.barrier()
             d("rope_apply", x=t["qn"], cos_table=t["rope.cos"], sin_table=t["rope.sin"], y=t["qr"],
               rows=T * c.heads, heads=c.heads, head_dim=c.head_dim, pos0=pos0)
             d("rope_apply", x=t["kn"], cos_table=t["rope.cos"], sin_table=t["rope.sin"], y=t["kr"],
               rows=T * c.kv_heads, heads=c.kv_heads, head_dim=c.head_dim, pos0=pos0)
+            tap(L + "attn.q_rope", "qr")
+            tap(L + "attn.k_rope", "kr")
             cl.barrier()
             d("copy_rows", src=t["kr"], dst=t[f"L{i}.k_cache"], rows=T, cols=kv, src_row0=0, dst_row0=pos0,
               src_stride=kv, dst_stride=kv)
             d("copy_rows", src=t["v"], dst=t[f"L{i}.v_cache"], rows=T, cols=kv, src_row0=0, dst_row0=pos0,
               src_stride=kv, dst_stride=kv)
+            if L + "attn.v_cache" in self.taps:  # the rows just appended to the cache
+                cl.barrier()
+                (ss, so), (ds, do) = self.place[f"L{i}.v_cache"], self.place["tap:" + L + "attn.v_cache"]
+                n = T * kv * 4
+                cl.copy(G.BufferRange(ss, so + pos0 * kv * 4, n), G.BufferRange(ds, do, n))
             cl.barrier()
             d("attention_gqa_causal", q=t["qr"], k=t[f"L{i}.k_cache"], v=t[f"L{i}.v_cache"], y=t["o"], rows=T,
               q_row0=0, past=pos0, q_heads=c.heads, kv_heads=c.kv_heads, head_dim=c.head_dim, scale=self.scale)
+            tap(L + "attn.o_proj.in", "o")
             cl.barrier()
             d("matmul_bf16w", x=t["o"], w=t[p + HF["o_proj"]], y=t["oo"], m=T, n=H, k=q)
+            tap(L + "attn.o_proj.out", "oo")
             cl.barrier()
             d("add", a=t["x"], b=t["oo"], y=t["r"], n=T * H)
+            tap(L + "resid_mid", "r")
             cl.barrier()
             d("rmsnorm_rows", x=t["r"], w=t[p + HF["post_attention_layernorm"]], y=t["h2"], rows=T, cols=H,
               eps=self.eps)
+            tap(L + "post_attention_layernorm.out", "h2")
             cl.barrier()
             d("matmul_bf16w", x=t["h2"], w=t[p + HF["gate_proj"]], y=t["g"], m=T, n=I, k=H)
             d("matmul_bf16w", x=t["h2"], w=t[p + HF["up_proj"]], y=t["u"], m=T, n=I, k=H)
+            tap(L + "mlp.gate.out", "g")
+            tap(L + "mlp.up.out", "u")
             cl.barrier()
             d("silu_mul", gate=t["g"], up=t["u"], y=t["d"], n=T * I)
+            tap(L + "mlp.down.in", "d")
             cl.barrier()
             d("matmul_bf16w", x=t["d"], w=t[p + HF["down_proj"]], y=t["dd"], m=T, n=H, k=I)
+            tap(L + "mlp.down.out", "dd")
             cl.barrier()
             d("add", a=t["r"], b=t["dd"], y=t["x"], n=T * H)
+            tap(L + "out", "x")
         cl.barrier()
         d("rmsnorm_rows", x=t["x"], w=t["model.norm.weight"], y=t["f"], rows=T, cols=H, eps=self.eps)
+        tap("final_norm.out", "f")
         cl.barrier()
         if logits_rows == "last":
             d("copy_rows", src=t["f"], dst=t["f_last"], rows=1, cols=H, src_row0=T - 1, dst_row0=0, src_stride=H,
@@ -213,6 +270,7 @@ class Fp32Executor:
         else:
             d("matmul_bf16w", x=t["f"], w=t["model.embed_tokens.weight"], y=t["logits"], m=T, n=c.vocab, k=H)
             rows = T
+        self._tap(cl, "logits", "logits", rows)
         cl.barrier()
         d("argmax_rows", x=t["logits"], y=t["next"], rows=rows, cols=c.vocab)
         return rows
@@ -231,7 +289,16 @@ class Fp32Executor:
         self.b.wait(self.b.submit(cl))
         logits = self.download("logits", np.float32, (rows, self.c.vocab))
         nxt = self.download("next", np.uint32, (rows,))
+        self._last = (T, rows)
         return logits, nxt
+
+    def read_taps(self) -> dict:
+        """The taps of the last forward: name -> float32 [T, cols] ([rows, vocab] for the logits)."""
+        if not self.taps:
+            raise RuntimeError("the executor was built without taps")
+        T, rows = self._last
+        return {name: self.download("tap:" + name, np.float32, (rows if name == "logits" else T, cols))
+                for name, (_, cols) in self.taps.items()}
 
     def greedy(self, prompt, steps: int, return_logits: bool = False):
         """TinyModel.greedy: prefill once, then single-token steps; argmax of each step's last row (a NaN row

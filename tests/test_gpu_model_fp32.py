@@ -90,3 +90,34 @@ def test_config1_fp32_greedy_and_logits():
     ref_ids, ref_logits = O.greedy(m, prompt, 16, "f32", return_logits=True)
     assert np.array_equal(ids, ref_ids)
     assert np.max(np.abs(logits - ref_logits)) <= 1e-4
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+@pytest.mark.parametrize("prompt", ["p0", "p1"])
+def test_tiny_taps_arena_equals_the_reference_taps(tiny_golden, prompt):
+    """Every intermediate of the forward, copied into the Taps arena at record time, against the reference's torch32
+    taps (goldens/tiny/g1 fwd_f32.*, rel-L2 <= 1e-5: the bar the CPU reference meets) and the CPU reference's own
+    taps (max-abs <= 1e-4)."""
+    cfg, weights, cos, sin = tiny_setup(tiny_golden)
+    b = CB.try_create()
+    try:
+        ex = X.Fp32Executor(b, cfg, weights, cos, sin, max_tokens=32, taps=True)
+        ex.reset_cache()
+        ids = tiny_golden[f"prompt/{prompt}"]
+        ex.forward(0, ids, "all")
+        got = ex.read_taps()
+    finally:
+        b.dispose()
+    m = oracle_model(cfg, weights, cos, sin)
+    ref = {}
+    O.forward(m, O.Cache.new(m.config, "f32"), 0, ids, "f32", ref)
+    assert len(got) == 39 and set(got) == set(ref)
+    for k, v in got.items():
+        assert v.shape == np.asarray(ref[k]).shape, k
+        assert rel_l2(v, tiny_golden[f"torch32/{prompt}/{k}"]) <= 1e-5, k
+        assert np.max(np.abs(v - ref[k])) <= 1e-4, k
