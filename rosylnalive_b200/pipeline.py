@@ -9,8 +9,9 @@ Two drivers over QwenEngine stages (QwenEngine(..., stage=(first, end))):
     each stage's input history, so rebuild(i, engine) replays it into a fresh engine: the same calls in the same
     order give the same KV cache bit for bit.
   * DistPipeline: one stage per rank of a torch.distributed group (one process per GPU, NCCL; gloo on CPU). Ranks
-    pass the residual rows forward and the last stage's next ids back to rank 0 with point-to-point send/recv, and
-    greedy() splits the sequences into microbatches so every stage works on one while the others work on the rest.
+    pass the residual rows forward and the last stage's next ids back to rank 0 with point-to-point transfers
+    between lockstep ticks, and the sequences run in microbatch groups so the stages work on different groups at
+    once.
 
 A split forward is bit-identical to the unsplit engine (the stages run the unsplit forward's kernels in its order),
 which tests/test_gpu_pipeline.py checks for prefill, decode and the replayed rebuild.
@@ -130,28 +131,29 @@ class LocalPipeline:
 class DistPipeline:
     """One stage per rank (rank r holds stage r of `world` stages); see the module docstring.
 
-    `engine` is this rank's stage. Every rank calls greedy() with the same arguments; rank 0 returns the ids, the
-    others None. Tensors travel with torch.distributed point-to-point calls on the default group (NCCL for CUDA
+    `engine` is this rank's stage. Every rank makes the same calls with the same arguments; rank 0 returns the ids,
+    the others None. Tensors travel with torch.distributed point-to-point calls on the default group (NCCL for CUDA
     engines, gloo for host ones); `device` is where the transfer buffers live.
 
-    No order of the ranks' progress can deadlock: sends are non-blocking (isend); rank 0 takes a microbatch's ids
-    from the last rank only right before it needs them for that microbatch's next step; and the residual rows
-    (forward) and the ids (back) travel on two process groups. One communicator runs a rank's point-to-point calls
-    in the order they were posted, so with a single group rank 0's queued residual sends would wait behind rank 1's
-    ids send, which waits for rank 0's ids receive behind those sends, once a message is too large to go eagerly.
-    Every rank constructs DistPipeline at the same point (the groups are created collectively)."""
+    The ranks run in lockstep ticks: at tick t, stage r runs call k of sequence group g when
+    t = k * max(M, W) + g + r (M groups, W stages), so a group's call moves one stage a tick and its next call
+    starts on stage 0 after the last stage has returned the ids it needs. Between ticks every rank posts all its
+    sends and receives of that exchange at once (batch_isend_irecv) and waits for them: residual rows to the next
+    stage, and the last stage's next ids to rank 0. No transfer is in flight while a stage computes. This matters:
+    a communication kernel waiting for its peer holds SMs, and the engine's persistent GEMMs size their grids to
+    every SM, so a transfer left waiting across a compute call (the last stage's ids send, with rank 0 still busy
+    prefilling) stalled that GPU's GEMM, and with it the peer's transfer: the two ranks hung."""
 
     def __init__(self, engine, rank: int, world: int, device):
         self.engine, self.rank, self.world, self.device = engine, rank, world, device
         if engine.is_first != (rank == 0) or engine.is_last != (rank == world - 1):
             raise ValueError(f"rank {rank} of {world} holds layers [{engine.first}, {engine.end})")
-        self._inflight = []
-        self._fwd = self._back = None
+        self._n = 0
+        self._next = np.zeros(0, np.uint32)
         if world > 1:
             import torch.distributed as dist
 
-            self._fwd = dist.new_group(list(range(world)))
-            self._back = dist.new_group(list(range(world)))
+            dist.barrier()  # every rank's communicator is up before the first point-to-point batch
 
     def _sync(self):
         import torch
@@ -159,58 +161,82 @@ class DistPipeline:
         if str(self.device).startswith("cuda"):
             torch.cuda.synchronize(self.device)
 
-    def _isend(self, t, dst, group):
-        import torch.distributed as dist
-
-        self._inflight = [(r, x) for r, x in self._inflight if not r.is_completed()]
-        self._inflight.append((dist.isend(t, dst, group=group), t))  # the tensor stays alive until sent
-
-    def _drain(self):
-        for req, _ in self._inflight:
-            req.wait()
-        self._inflight.clear()
-
-    def _run(self, kind, slots, lens, ids):
-        """One call of this rank's stage on one microbatch: receive its residual rows (ranks after 0), run the stage,
-        send the rows on (ranks before the last) or the next ids back to rank 0 (the last rank). Returns the next
-        ids when this rank is both first and last."""
-        import torch
-        import torch.distributed as dist
-
-        e = self.engine
-        rows = int(np.sum(lens)) if kind == "prefill" else len(slots)
-        if self.rank > 0:
-            buf = torch.empty((rows, e.cfg.hidden), dtype=torch.float32, device=self.device)
-            dist.recv(buf, self.rank - 1, group=self._fwd)
-            self._sync()
-            e.residual(rows).copy_(buf)
-            self._sync()
-        if kind == "prefill":
-            nxt, _ = e.prefill_stage(slots, lens, ids if self.rank == 0 else None)
-        else:
-            nxt, _ = e.decode(slots, ids if self.rank == 0 else None)
-        if not e.is_last:
-            out = e.residual(rows).clone()
-            self._sync()
-            self._isend(out, self.rank + 1, self._fwd)
-        elif self.world > 1:
-            back = torch.from_numpy(nxt.astype(np.int64)).to(self.device)
-            self._sync()
-            self._isend(back, 0, self._back)
-        return nxt
-
-    def _ids_back(self, n):
-        """Rank 0: the next ids of the oldest microbatch call whose ids it has not taken yet."""
-        import torch
-        import torch.distributed as dist
-
-        buf = torch.empty(n, dtype=torch.int64, device=self.device)
-        dist.recv(buf, self.world - 1, group=self._back)
-        return buf.cpu().numpy().astype(np.uint32)
-
     @staticmethod
     def _groups(n, microbatches):
         return [g for g in np.array_split(np.arange(n, dtype=np.int32), max(1, microbatches)) if len(g)]
+
+    def _execute(self, groups, kinds, lens=None, toks=None):
+        """Runs calls kinds[0], kinds[1], ... ("prefill" / "decode") for every sequence group through the stages in
+        lockstep ticks. lens[g] are group g's prompt lengths and toks[g] its prompts (rank 0) for a prefill; a
+        decode call of group g takes self._next[groups[g]] on rank 0. Rank 0 returns out[g][k], the next ids of
+        group g's call k, and keeps the latest in self._next."""
+        import torch
+        import torch.distributed as dist
+
+        W, M, C = self.world, len(groups), len(kinds)
+        Mp = max(M, W)
+        e = self.engine
+
+        def task(r, t):
+            u = t - r
+            if r < 0 or r >= W or u < 0:
+                return None
+            k, g = divmod(u, Mp)
+            return (g, k) if g < M and k < C else None
+
+        def rows_of(g, k):
+            return int(np.sum(lens[g])) if kinds[k] == "prefill" else len(groups[g])
+
+        out = [[None] * C for _ in range(M)]
+        inbox = None
+        for t in range((C - 1) * Mp + (M - 1) + (W - 1) + 1):
+            mine = task(self.rank, t)
+            nxt = None
+            if mine is not None:
+                g, k = mine
+                slots = groups[g]
+                if self.rank > 0:
+                    e.residual(inbox.shape[0]).copy_(inbox)
+                    self._sync()
+                if kinds[k] == "prefill":
+                    nxt, _ = e.prefill_stage(slots, lens[g], toks[g] if self.rank == 0 else None)
+                else:
+                    nxt, _ = e.decode(slots, self._next[slots] if self.rank == 0 else None)
+                if W == 1:
+                    self._next[slots] = nxt
+                    out[g][k] = nxt.copy()
+            if W == 1:
+                continue
+            # the exchange after tick t: all of this rank's sends and receives, posted together
+            ops, keep, idbuf, got = [], [], None, None
+            if mine is not None and self.rank < W - 1:
+                rows = e.residual(rows_of(*mine)).clone()
+                keep.append(rows)
+                ops.append(dist.P2POp(dist.isend, rows, self.rank + 1))
+            if mine is not None and self.rank == W - 1:
+                ids = torch.from_numpy(nxt.astype(np.int64)).to(self.device)
+                keep.append(ids)
+                ops.append(dist.P2POp(dist.isend, ids, 0))
+            prev = task(self.rank - 1, t)
+            if prev is not None:
+                inbox = torch.empty((rows_of(*prev), e.cfg.hidden), dtype=torch.float32, device=self.device)
+                ops.append(dist.P2POp(dist.irecv, inbox, self.rank - 1))
+            if self.rank == 0:
+                got = task(W - 1, t)
+                if got is not None:
+                    idbuf = torch.empty(len(groups[got[0]]), dtype=torch.int64, device=self.device)
+                    ops.append(dist.P2POp(dist.irecv, idbuf, W - 1))
+            if ops:
+                self._sync()
+                for req in dist.batch_isend_irecv(ops):
+                    req.wait()
+                self._sync()
+            if got is not None:
+                g, k = got
+                ids = idbuf.cpu().numpy().astype(np.uint32)
+                self._next[groups[g]] = ids
+                out[g][k] = ids
+        return out if self.rank == 0 else None
 
     def prefill(self, prompts, microbatches: int = 1):
         """Prefills `prompts` into slots 0..n-1 in `microbatches` groups (each stage runs group g while the next runs
@@ -218,48 +244,31 @@ class DistPipeline:
         self._n = len(prompts)
         self._next = np.zeros(self._n, np.uint32)
         groups = self._groups(self._n, microbatches)
-        for slots in groups:
-            lens = np.array([len(prompts[s]) for s in slots], np.int32)
-            toks = [np.asarray(prompts[s], np.uint32) for s in slots] if self.rank == 0 else None
-            r = self._run("prefill", slots, lens, toks)
-            if self.world == 1:
-                self._next[slots] = r
-        if self.rank == 0 and self.world > 1:
-            for slots in groups:
-                self._next[slots] = self._ids_back(len(slots))
+        lens = [np.array([len(prompts[s]) for s in slots], np.int32) for slots in groups]
+        toks = [[np.asarray(prompts[s], np.uint32) for s in slots] for slots in groups] if self.rank == 0 else None
+        self._execute(groups, ["prefill"], lens, toks)
         return self._next.copy() if self.rank == 0 else None
 
     def decode_steps(self, steps: int, microbatches: int = 2):
-        """`steps` greedy decode steps of every prefilled sequence, in `microbatches` groups: rank 0 feeds group g's
-        step s with the ids of its step s - 1 as soon as the last rank sends them, so the stages overlap. Returns ids
-        [n, steps] on rank 0, None elsewhere."""
+        """`steps` greedy decode steps of every prefilled sequence, in `microbatches` groups (the stages work on
+        different groups at once once there are at least as many groups as stages). Returns ids [n, steps] on rank
+        0, None elsewhere."""
         groups = self._groups(self._n, microbatches)
-        out = np.zeros((self._n, steps), np.int64) if self.rank == 0 else None
-        for s in range(steps):
-            for slots in groups:
-                ids = None
-                if self.rank == 0:
-                    ids = self._next[slots] if (s == 0 or self.world == 1) else self._ids_back(len(slots))
-                    if s > 0 and self.world > 1:
-                        out[slots, s - 1] = ids
-                        self._next[slots] = ids
-                r = self._run("decode", slots, None, ids)
-                if self.world == 1:
-                    self._next[slots] = r
-                    out[slots, s] = r
-        if self.rank == 0 and self.world > 1 and steps > 0:
-            for slots in groups:
-                self._next[slots] = self._ids_back(len(slots))
-                out[slots, steps - 1] = self._next[slots]
-        self._drain()
-        return out
+        if steps < 1:
+            return np.zeros((self._n, 0), np.int64) if self.rank == 0 else None
+        out = self._execute(groups, ["decode"] * steps)
+        if self.rank != 0:
+            return None
+        ids = np.zeros((self._n, steps), np.int64)
+        for g, slots in enumerate(groups):
+            ids[slots] = np.stack(out[g], 1)
+        return ids
 
     def greedy(self, prompts, steps: int, microbatches: int = 2):
         """QwenEngine.greedy through the pipeline: prefill, then steps - 1 decode steps, sequences in
         `microbatches` groups. Returns ids [n, steps] on rank 0, None elsewhere."""
         first = self.prefill(prompts, microbatches)
         rest = self.decode_steps(steps - 1, microbatches) if steps > 1 else None
-        self._drain()
         if self.rank != 0:
             return None
         cols = [first.astype(np.int64)[:, None]] + ([rest] if rest is not None else [])
