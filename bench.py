@@ -354,7 +354,7 @@ def run_ours(args, dist):
 
 
 def run_pipeline(args, dist):
-    """The pipeline stage split (SURVEY-scope row "serving / pipeline stage split"; not the headline): rank r holds
+    """The pipeline stage split (the reference's planned StagePipeline; not the headline): rank r holds
     stage r of the 28 layers (rosylnalive_b200.pipeline.split_layers) for all B x N sequences; the fp32 residual
     crosses ranks with NCCL send/recv, the next ids return to rank 0, and the sequences run in `microbatches` groups
     so the stages work concurrently. Setup prefills the KV caches through the same pipeline; the timed region is
