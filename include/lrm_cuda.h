@@ -303,7 +303,10 @@ lrm_status lrm_qwen_extend(lrm_qwen q, int32_t nseq, const int32_t *slots, const
 lrm_status lrm_qwen_decode(lrm_qwen q, int32_t batch, const int32_t *slots, const uint32_t *ids, uint32_t *next_ids,
                            float *logits);
 
-/* Captures the decode step for `slots` as a CUDA graph whose input ids are the previous step's outputs. With
+/* Captures the decode step for `slots` as a CUDA graph whose input ids are the previous step's outputs (a
+ * pipeline stage's graph reads its inputs as lrm_qwen_decode supplies them). The engine keeps the 8 most recent
+ * captures by slot list; lrm_qwen_decode replays the one whose slots match its call, and the most recent one is
+ * what lrm_qwen_decode_replay, lrm_qwen_last_ids and the attention timers use. With
  * LRM_QWEN_GRAPH_TIME_ATTENTION in flags, the graph also records CUDA events around every layer's decode attention,
  * read back by lrm_qwen_attention_ms after a replay. */
 #define LRM_QWEN_GRAPH_TIME_ATTENTION 0x1u

@@ -97,7 +97,13 @@ struct lrm_qwen_s {
     size_t partial_elems = 0;
     int max_splits_attn = 0;
     int pps = 32;
-    // decode graph
+    // decode graphs: the most recent capture (replay, last ids, timers) and every kept capture by slot set
+    struct KeptGraph {
+        std::vector<int32_t> slots;
+        cudaGraphExec_t exec;
+    };
+    static constexpr size_t kKeptGraphs = 8;
+    std::vector<KeptGraph> kept;
     cudaGraphExec_t graph = nullptr;
     int graph_batch = 0;
     int graph_kernels = 0;
@@ -413,7 +419,7 @@ lrm_status lrm_qwen_destroy(lrm_qwen Q) {
     if (!Q) return LRM_ERR_ARGUMENT;
     cudaSetDevice(Q->device);
     cudaStreamSynchronize(Q->stream);
-    if (Q->graph) cudaGraphExecDestroy(Q->graph);
+    for (auto &k : Q->kept) cudaGraphExecDestroy(k.exec);
     for (auto e : Q->attn_ev) cudaEventDestroy(e);
     cudaFree(Q->wmem);
     cudaFree(Q->cos_t);
@@ -787,10 +793,11 @@ lrm_status lrm_qwen_decode(lrm_qwen Q, int32_t batch, const int32_t *slots, cons
         memcpy(Q->h_pinned, ids, 4 * (size_t)batch);
         QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, st), "ids");
     }
-    const bool use_graph = Q->graph && Q->graph_batch == batch &&
-                           std::equal(Q->graph_slots.begin(), Q->graph_slots.end(), slots);
+    cudaGraphExec_t use_graph = nullptr;  // a kept capture of this exact slot list, if any
+    for (const auto &k : Q->kept)
+        if ((int)k.slots.size() == batch && std::equal(k.slots.begin(), k.slots.end(), slots)) use_graph = k.exec;
     if (use_graph) {
-        QTRY(Q, cudaGraphLaunch(Q->graph, st), "graph launch");
+        QTRY(Q, cudaGraphLaunch(use_graph, st), "graph launch");
     } else {
         LTRY(decode_step(Q, batch));
     }
@@ -821,10 +828,18 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
         QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, Q->stream), "ids");
     }
     LTRY(sync_check(Q));
-    if (Q->graph) {
-        cudaGraphExecDestroy(Q->graph);
-        Q->graph = nullptr;
+    // a new capture replaces one of the same slot list, else the oldest once kKeptGraphs are kept
+    for (size_t i = 0; i < Q->kept.size(); ++i)
+        if ((int)Q->kept[i].slots.size() == batch && std::equal(Q->kept[i].slots.begin(), Q->kept[i].slots.end(), slots)) {
+            cudaGraphExecDestroy(Q->kept[i].exec);
+            Q->kept.erase(Q->kept.begin() + i);
+            break;
+        }
+    if (Q->kept.size() >= lrm_qwen_s::kKeptGraphs) {
+        cudaGraphExecDestroy(Q->kept.front().exec);
+        Q->kept.erase(Q->kept.begin());
     }
+    Q->graph = nullptr;
     cudaGraph_t g;
     QTRY(Q, cudaStreamBeginCapture(Q->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     lrm_status s = decode_step(Q, batch, timed);
@@ -847,6 +862,7 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
     e = cudaGraphInstantiate(&Q->graph, g, 0);
     cudaGraphDestroy(g);
     QTRY(Q, e, "graph instantiate");
+    Q->kept.push_back({std::vector<int32_t>(slots, slots + batch), Q->graph});
     Q->graph_kernels = kernels;
     Q->graph_timed = timed;
     Q->graph_batch = batch;

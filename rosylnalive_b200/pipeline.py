@@ -150,6 +150,7 @@ class DistPipeline:
             raise ValueError(f"rank {rank} of {world} holds layers [{engine.first}, {engine.end})")
         self._n = 0
         self._next = np.zeros(0, np.uint32)
+        self._captured = set()
         if world > 1:
             import torch.distributed as dist
 
@@ -256,6 +257,12 @@ class DistPipeline:
         groups = self._groups(self._n, microbatches)
         if steps < 1:
             return np.zeros((self._n, 0), np.int64) if self.rank == 0 else None
+        if hasattr(self.engine, "capture"):  # one decode graph per group, replayed by the engine's decode calls
+            for slots in groups:
+                key = tuple(int(x) for x in slots)
+                if key not in self._captured:
+                    self.engine.capture(slots)
+                    self._captured.add(key)
         out = self._execute(groups, ["decode"] * steps)
         if self.rank != 0:
             return None

@@ -219,3 +219,29 @@ def test_extend_is_checked(mini):
     with pytest.raises(ValueError):  # a slot twice
         eng.extend([6, 6], [np.zeros(2, np.uint32), np.zeros(2, np.uint32)])
     assert eng.seq_len(6) == 10
+
+
+def test_kept_graphs_serve_alternating_slot_sets(mini):
+    """Two captured slot sets used in turn (as a pipeline's microbatches are): every call replays its own graph and
+    gives eager decode's logits bit for bit."""
+    cfg, om, eng = mini
+    prompts = [S.random_prompt(cfg.vocab, 30 + 7 * i, seed=60 + i, stream=f"k{i}") for i in range(4)]
+    a, b = [0, 1], [2, 3]
+
+    def run(capture):
+        first, _ = eng.prefill([0, 1, 2, 3], prompts)
+        ids = {0: first[:2], 1: first[2:]}
+        if capture:
+            eng.capture(a)
+            eng.capture(b)
+        got = []
+        for _ in range(3):
+            for k, slots in ((0, a), (1, b)):
+                nxt, lg = eng.decode(slots, ids[k], want_logits=True)
+                ids[k] = nxt
+                got.append(lg.copy())
+        return np.stack(got)
+
+    eager = run(False)
+    graphs = run(True)
+    assert np.array_equal(eager.view(np.uint32), graphs.view(np.uint32))
