@@ -146,6 +146,35 @@ __global__ void __launch_bounds__(256) norm_rows_warp_kernel(const float *x, int
     }
 }
 
+// The same with a compile-time row width (N4 float4s, hidden 4 N4): every lane issues its N4 / 32 row loads at once
+// and keeps them in registers for the second pass. The sums run in the same order, so the results are the same bits.
+template <int N4>
+__global__ void __launch_bounds__(256) norm_rows_warp_fixed_kernel(const float *x, int T, const __nv_bfloat16 *w,
+                                                                   float eps, __nv_bfloat16 *xn) {
+    static_assert(N4 % 32 == 0, "a whole number of float4s a lane");
+    constexpr int PER = N4 / 32;
+    ptx::griddep_wait();
+    ptx::griddep_launch();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * N4 * 4);
+    float4 v[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] = xr[lane + 32 * i];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    const float r = rsqrtf(warp_sum(ss) / (N4 * 4) + eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int c = lane + 32 * i;
+        const uint2 wv = *reinterpret_cast<const uint2 *>(w + 4 * c);
+        *reinterpret_cast<uint2 *>(xn + (size_t)row * N4 * 4 + 4 * c) =
+            pack4(v[i].x * r * __uint_as_float(wv.x << 16), v[i].y * r * __uint_as_float(wv.x & 0xFFFF0000u),
+                  v[i].z * r * __uint_as_float(wv.y << 16), v[i].w * r * __uint_as_float(wv.y & 0xFFFF0000u));
+    }
+}
+
 // ---- q/k norm + RoPE + KV append --------------------------------------------------------------------------------
 
 // One warp per (token, head row); lane l owns dims 4l..4l+3. Head rows 0..q-1 are q, then kv k rows, then kv v rows.
@@ -521,9 +550,13 @@ cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *e
 
 cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
                               const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st) {
-    if (splits == 0)
+    if (splits == 0) {
+        if (hidden == 1024)  // Qwen3-0.6B
+            return launch_kernel(norm_rows_warp_fixed_kernel<256>, dim3((T + 7) / 8), dim3(256), 0, st,
+                                 (const float *)x, T, w, eps, xn);
         return launch_kernel(norm_rows_warp_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float *)x, T, hidden,
                              w, eps, xn);
+    }
     return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, partial, splits, split_stride, hidden, w,
                          eps, xn);
 }
