@@ -593,7 +593,7 @@ cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_
 }
 
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
-    constexpr int ST = 4;  // 37 KiB of shared memory a CTA, five CTAs an SM (measured faster than 8 / 12 / 16)
+    constexpr int ST = 4;  // 37 KiB of shared memory a CTA, six CTAs an SM (measured faster than 8 / 12 / 16)
     const size_t smem = ST * 8192 + (4 * 32 + 4 * 2 * 128 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
     static bool configured[64] = {};
     int dev = 0;
