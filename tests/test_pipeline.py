@@ -118,17 +118,38 @@ def free_port():
 PROMPTS = [[(7 * i + 3 * k) % VOCAB for k in range(3 + i)] for i in range(6)]
 
 
-def _rank_main(rank, world, port, steps, microbatches, q):
+class FailingStage(FakeStage):
+    """A stage whose host raises on its `fail_at`-th call (a stage process that dies between ticks)."""
+
+    def __init__(self, first, end, fail_at):
+        super().__init__(first, end)
+        self.fail_at = fail_at
+
+    def _check(self):
+        if self.calls + 1 == self.fail_at:
+            raise RuntimeError(f"stage [{self.first}, {self.end}) failed at call {self.fail_at}")
+
+    def prefill_stage(self, *args, **kw):
+        self._check()
+        return super().prefill_stage(*args, **kw)
+
+    def decode(self, *args, **kw):
+        self._check()
+        return super().decode(*args, **kw)
+
+
+def _rank_main(rank, world, port, steps, microbatches, q, fail=None):
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
     sys.path.insert(0, ROOT)
     import datetime
 
     import torch.distributed as dist
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    timeout = datetime.timedelta(seconds=5 if fail else 60)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
     try:
         first, end = PL.split_layers(LAYERS, world)[rank]
-        eng = FakeStage(first, end)
+        eng = FailingStage(first, end, fail[1]) if fail and fail[0] == rank else FakeStage(first, end)
         pipe = PL.DistPipeline(eng, rank, world, "cpu")
         ids = pipe.greedy(PROMPTS, steps, microbatches)
         q.put((rank, "ok", None if ids is None else ids.tolist(), eng.calls))
@@ -138,11 +159,12 @@ def _rank_main(rank, world, port, steps, microbatches, q):
         dist.destroy_process_group()
 
 
-def run_pipeline(world, steps, microbatches, timeout=120):
+def run_pipeline(world, steps, microbatches, timeout=120, fail=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, steps, microbatches, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, steps, microbatches, q, fail))
+             for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -204,3 +226,16 @@ def test_dist_pipeline_rejects_a_stage_on_the_wrong_rank():
         PL.DistPipeline(FakeStage(0, 3), 1, 2, "cpu")
     with pytest.raises(ValueError):
         PL.DistPipeline(FakeStage(3, LAYERS), 0, 2, "cpu")
+
+
+@pytest.mark.parametrize("fail_rank", [0, 1])
+def test_a_failing_stage_ends_the_other_ranks_with_an_error(fail_rank):
+    """A stage that raises between ticks (its process then leaves) makes the other rank's next exchange fail on the
+    host (peer gone, or the 5 s process-group timeout) instead of hanging; no rank returns ids."""
+    t0 = time.time()
+    out = run_pipeline(2, 5, 2, timeout=90, fail=(fail_rank, 3))
+    assert time.time() - t0 < 90
+    assert sorted(out) == [0, 1], out
+    assert out[fail_rank][0] == "error" and "failed at call 3" in out[fail_rank][1], out
+    other = 1 - fail_rank
+    assert out[other][0] == "error", out
