@@ -130,13 +130,22 @@ static lrm_status qcuda(lrm_qwen q, cudaError_t e, const char *what) {
         if (e_ != cudaSuccess) return qcuda(q, e_, what); \
     } while (0)
 
-// Split counts for the decode GEMMs: enough CTAs to stream each weight matrix with ~all SMs.
+// Split counts for the decode GEMMs: the fewest k-blocks on the busiest SM. A launch runs min(tiles, sms) CTAs that
+// take the m_tiles x s tiles round robin, so s splits cost waves(m_tiles * s) x ceil(kb / s) k-blocks; ties go to
+// fewer splits (fewer partials for the consumer to reduce). No split may be empty.
 static int choose_splits(int m_tiles, int kb, int sms) {
-    int s = (sms + m_tiles - 1) / m_tiles;
-    if (s > kb) s = kb;
-    if (s < 1) s = 1;
-    while (s > 1 && (kb + s - 1) / s * (s - 1) >= kb) --s;  // no empty split
-    return s;
+    int best = 1;
+    long best_cost = -1;
+    for (int s = 1; s <= kb; ++s) {
+        const int per = (kb + s - 1) / s;
+        if (per * (s - 1) >= kb) continue;  // the last split would be empty
+        const long cost = (((long)m_tiles * s + sms - 1) / sms) * per;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    return best;
 }
 
 static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, int K, int epi, int bn, int splits,
@@ -172,6 +181,8 @@ static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, i
     };
     a.independent = is_weight(A) ? 1 : (is_weight(B) ? 2 : 0);
     if (const char *why = gemm_check(a)) return qfail(Q, LRM_ERR_ARGUMENT, std::string("gemm: ") + why);
+    if (epi == EPI_PARTIAL && out == Q->partial && (size_t)splits * split_stride > Q->partial_elems)
+        return qfail(Q, LRM_ERR_STATE, "gemm: the split-K partials do not fit the partial buffer");
     return qcuda(Q, gemm_launch(a, Q->sms, Q->stream), "gemm");
 }
 
