@@ -529,14 +529,38 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
     const int npages = (len + kPageTokens - 1) / kPageTokens;
     const int nsplit = (npages + a.pages_per_split - 1) / a.pages_per_split;
     const size_t base = ((size_t)b * a.kv.kv_heads + h) * a.max_splits;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, a.part_ml[((base + s) * 2 + hh) * 2]);
-    float o = 0.f, l = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-        const float m = a.part_ml[((base + s) * 2 + hh) * 2];
-        const float f = m == -INFINITY ? 0.f : exp2f(m - M);
-        o += f * a.part_o[((base + s) * 2 + hh) * 128 + d];
-        l += f * a.part_ml[((base + s) * 2 + hh) * 2 + 1];
+    const float *ml = a.part_ml + (base * 2 + hh) * 2;    // split s: ml[4 s] = max, ml[4 s + 1] = sum
+    const float *po = a.part_o + (base * 2 + hh) * 128 + d;  // split s: po[256 s]
+    float M = -INFINITY, o = 0.f, l = 0.f;
+    constexpr int kHeld = 16;
+    if (nsplit <= kHeld) {
+        // every split's state is loaded before any is used, so the loads are in flight together
+        float mv[kHeld], lv[kHeld], ov[kHeld];
+#pragma unroll
+        for (int s = 0; s < kHeld; ++s)
+            if (s < nsplit) {
+                mv[s] = ml[4 * s];
+                lv[s] = ml[4 * s + 1];
+                ov[s] = po[256 * s];
+            }
+#pragma unroll
+        for (int s = 0; s < kHeld; ++s)
+            if (s < nsplit) M = fmaxf(M, mv[s]);
+#pragma unroll
+        for (int s = 0; s < kHeld; ++s)
+            if (s < nsplit) {
+                const float f = mv[s] == -INFINITY ? 0.f : exp2f(mv[s] - M);
+                o += f * ov[s];
+                l += f * lv[s];
+            }
+    } else {
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[4 * s]);
+        for (int s = 0; s < nsplit; ++s) {
+            const float m = ml[4 * s];
+            const float f = m == -INFINITY ? 0.f : exp2f(m - M);
+            o += f * po[256 * s];
+            l += f * ml[4 * s + 1];
+        }
     }
     a.out[((size_t)b * a.q_heads + qh) * kHeadDim + d] = __float2bfloat16_rn(o / l);
 }
