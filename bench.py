@@ -184,6 +184,17 @@ def cpu_decode_sample(weights, cfg, context, seconds, max_steps=None):
     return n / dt, n, dt, O.THREADS
 
 
+def decode_config(B, ctx, world, layers):
+    """The config-5 workload both arms report: our arm runs it whole, the reference arm times a bounded sample of it
+    (described in its cpu_baseline.sample)."""
+    return {"workload": f"config5: Qwen3-0.6B bf16 greedy decode, {B} seqs/GPU, {ctx}-token paged KV "
+                        "(16-token pages), random-init weights N(0,0.02), random prompt ids"
+                        + ("" if layers == 28 else f" [profiling case: {layers} layers]"),
+            "model": "Qwen3-0.6B architecture", "global_batch": B * world, "seq_len": ctx,
+            "parallelism": f"dp{world} (independent sequences per GPU, no collective)",
+            "l2": "inputs larger than L2 (32 GB KV cache), no flush"}
+
+
 def run_reference(args, dist):
     from rosylnalive_b200 import synthetic as S
 
@@ -198,8 +209,7 @@ def run_reference(args, dist):
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": n, "warmup": args.warmup, "ms_per_step": 1000 * dt / n, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config5-sample: Qwen3-0.6B greedy decode, CPU reference, 1 sequence",
-                       "seq_len": args.context},
+            "config": decode_config(args.batch, args.context, args.gpus, cfg.layers),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -341,12 +351,7 @@ def run_ours(args, dist):
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": K, "warmup": W,
                 "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": f"config5: Qwen3-0.6B bf16 greedy decode, {B} seqs/GPU, {ctx}-token paged KV "
-                                       "(16-token pages), random-init weights N(0,0.02), random prompt ids"
-                                       + ("" if cfg.layers == 28 else f" [profiling case: {cfg.layers} layers]"),
-                           "model": "Qwen3-0.6B architecture", "global_batch": B * dist.world, "seq_len": ctx,
-                           "parallelism": f"dp{dist.world} (independent sequences per GPU, no collective)",
-                           "l2": "inputs larger than L2 (32 GB KV cache), no flush"},
+                "config": decode_config(B, ctx, dist.world, cfg.layers),
                 "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
                 "gpu_launches": launches_per_step * K * dist.world, "roofline": roofline, "step_roofline": step_roof,
                 "prefill": prefill, "cpu_baseline": cpu, "clocks": clocks}
