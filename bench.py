@@ -159,11 +159,11 @@ def cpu_decode_sample(weights, cfg, context, seconds, max_steps=None):
     """Times CPU-reference decode steps of one sequence at `context` cached tokens (fp32 cache filled with random
     values: the cost of a step does not depend on them). Returns (tok/s, steps, seconds, threads)."""
     from oracle import oracle as O
-    from rosylnalive_b200 import rope as R
+    from rosylnalive_b200.rope import QWEN3_INV_FREQ_BITS  # a constant: nothing of liblrmcuda is loaded here
 
     steps_cap = max_steps or 10 ** 6
     max_pos = context + min(steps_cap, 4096) + 1
-    cos, sin = R.t_spec(R.QWEN3_INV_FREQ_BITS, max_pos)
+    cos, sin = O.rope_table(QWEN3_INV_FREQ_BITS, max_pos)  # the oracle's own T_spec builder
     oc = O.Config(cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate, cfg.vocab, cfg.eps,
                   max_pos)
     m = O.Model.from_hf(oc, weights, cos, sin)

@@ -166,8 +166,18 @@ lrm_status lrm_cuda_timer_end(lrm_cmdlist list, uint32_t timer_id);
 /* Makes `device` current for the calling thread and initialises its operator state. */
 lrm_status lrm_op_set_device(int32_t device);
 
-/* Reads the current device's error word (0 = no kernel reported a timeout); clears it when `clear` != 0. */
+/* Reads the current device's error word (0 = no kernel reported an error); clears it when `clear` != 0. Codes:
+ * 0x1xxx, 0x2001-0x2003, 0x3xxx a bounded wait that gave up (GEMM, decode attention, prefill attention);
+ * 0x2010 a decode-attention row whose seq_len is below 1 or needs more pages than its page-table row (the row is
+ * not read and its output is zeros). */
 lrm_status lrm_op_error_word(uint32_t *code, int32_t clear);
+
+/* Runs one kernel whose bounded in-kernel wait can never complete (an mbarrier nothing arrives on), with a limit of
+ * `polls` polls (1 .. 2^24; the kernels' own limit is 2^24): the wait gives up, `code` (nonzero) lands in the error
+ * word and the kernel returns, leaving the device usable. It exists to test the path every kernel of this library
+ * takes when a wait runs out, the CUDA counterpart of the reference's device wait timeout
+ * (src/Lrm.Gpu.D3D12/Backend.fs:109, Context.fs:200-234), without hanging or faulting a GPU. */
+lrm_status lrm_op_wait_probe(void *stream, uint32_t polls, uint32_t code);
 
 #define LRM_GEMM_F32 0     /* out_f32[m, n] = acc */
 #define LRM_GEMM_RESID 1   /* out_f32[m, n] = resid[m, n] + acc (resid may equal out) */
@@ -221,14 +231,16 @@ uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int3
 lrm_status lrm_op_decode_attention(void *stream, const lrm_decode_attn_desc *desc);
 
 /* Decode attention that allocates nothing. No counterpart in the reference: it is for callers that cannot allocate
- * device memory (a host that sizes all device memory once up front, as the reference's device contract does with
- * its one CreateHeap; a serving loop with a fixed memory budget; code inside a stream capture or a host callback),
- * and so cannot provide lrm_op_decode_attention's workspace. It runs the same kernels with their split-K scratch in
+ * device memory (a host that sizes all of its device memory once up front and never allocates per call; a serving
+ * loop with a fixed memory budget; code inside a stream capture or a host callback, where cudaMalloc is not
+ * allowed), and so cannot provide lrm_op_decode_attention's workspace. It runs the same kernels with their split-K scratch in
  * a 16 MiB array built into the library (every GPU that loads the library holds it until the process exits).
  * desc->workspace must be 0. A call needing more than LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES of scratch
  * (lrm_op_decode_attention_workspace) is refused with LRM_ERR_ARGUMENT. The first call on a device looks up the
  * array's device address with that device current; make it before any stream capture. Nothing in the scratch must
- * start at zero. All calls on a device share the array, so calls that overlap on the GPU race on it. */
+ * start at zero. All calls on a device share the array, so calls that overlap on the GPU race on it. The address is
+ * kept for the life of the process: after cudaDeviceReset (or any loss of the device's context) it is stale, as is
+ * the device's error word, so a process that resets a device must not call the library's operators on it again. */
 #define LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES (16u << 20)
 lrm_status lrm_op_decode_attention_static(void *stream, const lrm_decode_attn_desc *desc);
 

@@ -1,8 +1,8 @@
 // decode_attn_static.cu -- decode attention for callers that cannot allocate device memory.
 //
-// Who needs it: a host that follows the reference's device contract owns all of its device memory up front
-// (IGpuBackend.CreateHeap is called exactly once; a dispatch never allocates), a serving loop whose memory budget is
-// fixed after warm-up, code running inside a stream capture or a host callback (where cudaMalloc is not allowed).
+// Who needs it: a host that sizes all of its device memory once up front and never allocates per call, a serving
+// loop whose memory budget is fixed after warm-up, code running inside a stream capture or a host callback (where
+// cudaMalloc is not allowed).
 // Such a caller can pass the inputs and the output but has no way to provide the split-K scratch that
 // lrm_op_decode_attention takes as `workspace`. This entry point runs the same kernels with that scratch in a
 // fixed array inside this library:
@@ -11,7 +11,9 @@
 //     (LRM_ERR_ARGUMENT) before anything is launched;
 //   - host code cannot use the array's name as a device address (on the host it names a stand-in object), so the
 //     first call on each device, with that device current, asks the runtime for the address with
-//     cudaGetSymbolAddress and caches it per device; make that first call before any stream capture;
+//     cudaGetSymbolAddress and caches it per device for the life of the process; make that first call before any
+//     stream capture. A device reset (cudaDeviceReset) makes the cached address stale, so a process that resets a
+//     device must not call this entry point on it again;
 //   - nothing in the scratch has to start at zero: the combine kernel reads only the split states that the attention
 //     kernel of the same call has just written;
 //   - every call on a device shares the one array and it keeps the last call's contents, so calls that overlap on

@@ -46,13 +46,6 @@ constexpr int kRegsLaunch = 168;    // 65536 / 384, rounded down to the allocati
 constexpr int kRegsControl = 56, kRegsSoftmax = 224;
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split exceeds the launch");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-#ifndef LRM_FLASH_EMU_EVERY
-#define LRM_FLASH_EMU_EVERY 0
-#endif
-// On tiles without masking, every kEmuEvery-th pair of keys takes 2^x from a polynomial on the FMA pipe instead of
-// the transcendental unit, which two softmax warpgroups otherwise saturate (0: never).
-constexpr int kEmuEvery = LRM_FLASH_EMU_EVERY;
-
 struct FlashTcParams {
     const int32_t *cu_seqlens;
     __nv_bfloat16 *out;
@@ -88,29 +81,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     float r;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
     return r;
-}
-
-// 2^x for a pair on the FMA pipe, taking load off the transcendental unit: x = r + f with r = rint(x) (adding
-// 1.5 * 2^23 leaves the integer in the low mantissa bits) and f in [-1/2, 1/2]; 2^f is a degree-4 polynomial fitted
-// here for relative error on [-1/2, 1/2] (2.7e-6 at most in fp32 Horner form, against 2^-9 for the bf16 rounding of
-// P that follows); 2^r enters by adding r to the exponent field (1.5 * 2^23 << 23 vanishes mod 2^32). x is clamped
-// at -126 so the exponent field stays non-negative; masked keys (-inf) never take this path.
-constexpr float kE0 = 0.9999992847442627f, kE1 = 0.6931217908859253f, kE2 = 0.240247443318367f,
-                kE3 = 0.05591784045100212f, kE4 = 0.00957008171826601f;
-__device__ __forceinline__ void exp2_poly2(float &y0, float &y1, float x0, float x1) {
-    constexpr float kRound = 12582912.0f;
-    x0 = fmaxf(x0, -126.0f);
-    x1 = fmaxf(x1, -126.0f);
-    float t0, t1, r0, r1, f0, f1, p0, p1;
-    add2(t0, t1, x0, x1, kRound, kRound);
-    add2(r0, r1, t0, t1, -kRound, -kRound);
-    fma2(f0, f1, r0, r1, -1.0f, -1.0f, x0, x1);
-    fma2(p0, p1, kE4, kE4, f0, f1, kE3, kE3);
-    fma2(p0, p1, p0, p1, f0, f1, kE2, kE2);
-    fma2(p0, p1, p0, p1, f0, f1, kE1, kE1);
-    fma2(p0, p1, p0, p1, f0, f1, kE0, kE0);
-    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -377,12 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 64; ++e) {
                         float a, b;
                         fma2(a, b, x[2 * e], x[2 * e + 1], sc, sc, nm, nm);
-                        if (kEmuEvery > 0 && e % kEmuEvery == kEmuEvery - 1) {
-                            exp2_poly2(a, b, a, b);
-                        } else {
-                            a = ptx::ex2(a);
-                            b = ptx::ex2(b);
-                        }
+                        a = ptx::ex2(a);
+                        b = ptx::ex2(b);
                         if (e & 1)
                             add2(lc, ld, lc, ld, a, b);
                         else
@@ -488,14 +454,8 @@ cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_toke
                !make_tmap_heads(&tv, a.v, a.kv_heads, total_tokens)) {
         return cudaErrorInvalidValue;
     }
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!configured[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured[dev & 63] = true;
-    }
+    static SmemOptIn opt;
+    if (cudaError_t e = opt.set((const void *)flash_tc_kernel, SMEM_BYTES)) return e;
     FlashTcParams p;
     p.cu_seqlens = a.cu_seqlens;
     p.out = a.out;

@@ -1,6 +1,7 @@
 // gemm.h -- the tcgen05 GEMM's arguments (internal).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -50,6 +51,61 @@ struct GemmArgs {
     // tcgen05 cta_group::2 MMAs (bn 256, one split, not EPI_PARTIAL).
     int cta_pair;
 };
+
+// ---- decode GEMMs with their consumers fused (gemm_decode.cu) ----------------------------------------------------
+//
+// Y = A * B^T with A the weights [M, K] (M in 128-row tiles) and B the step's tokens [N, K] (N in 64-token tiles).
+// S CTAs (one cluster) split K for one output tile; they reduce their accumulators through distributed shared memory
+// in split order, and each finishes a share of the tile's tokens with the epilogue. B is a token's activation before
+// its RMSNorm scale: B[t] = bf16(gain * x[t]); the scale r[t] = 1 / sqrt(sum_g ss[g][t] / hidden + eps) is applied to
+// the output rows (the GEMM is linear in each token), so no kernel has to finish a whole row's norm before the GEMM.
+enum DecodeEpi : int {
+    DEC_QKV = 0,     // y = r * acc per head row (q heads, then k, then v): q/k get the per-head RMSNorm and RoPE; q to
+                     // q_out [N][q_heads][128], k and v into the paged cache at (tok_slot[t], tok_pos[t])
+    DEC_SWIGLU = 1,  // tile rows 0..63 gate j, 64..127 up j (64-row interleave): act[t][64 mt + j] = bf16(silu(r g) r u)
+    DEC_RESID = 2,   // x[t][m] += acc; with gain: u[t][m] = bf16(gain[m] x[t][m]) and ss_out[m / 128][t] = the sum of
+                     // x[t][m]^2 over the tile's 128 rows (decode_group_ss), the next GEMM's B and norm inputs
+};
+
+struct DecodeGemmArgs {
+    int M, N, K;
+    const void *A, *B;
+    int epi;
+    int splits, kb_per_split;  // S CTAs of a cluster split the K blocks (64 wide): kb_per_split each
+    // the norm scale of B's rows (null: 1)
+    const float *ss;
+    int nss, hidden;
+    size_t ss_stride;  // elements between groups of ss (and of ss_out)
+    float eps;
+    // DEC_RESID
+    float *x;
+    __nv_bfloat16 *u;
+    const __nv_bfloat16 *gain;  // null: x only
+    float *ss_out;
+    // DEC_SWIGLU
+    __nv_bfloat16 *act;
+    int ld_act;
+    // DEC_QKV (fields as QkvEpilogue)
+    QkvEpilogue qkv;
+    uint32_t *err;
+};
+
+const char *decode_gemm_check(const DecodeGemmArgs &a);
+cudaError_t decode_gemm_launch(const DecodeGemmArgs &a, cudaStream_t stream);
+// The split count for an M x K weight: clusters of at most 8 CTAs, at most one CTA an SM for one 64-token tile,
+// every split at most kDecodeStages k blocks when possible (all of a CTA's weights are fetched before it waits).
+int decode_gemm_splits(int M, int K, int sms);
+
+// The decode step's norm inputs from the residual stream, as DEC_RESID writes them: u[t] = bf16(gain * x[t]) and
+// ss[g][t] for 128-column groups g. With ids, x[t] = widen(embed[ids[t]]) is written first (a quiet NaN row for an id
+// outside the vocabulary).
+cudaError_t launch_decode_prep(const uint32_t *ids, const __nv_bfloat16 *embed, int vocab, float *x, int T,
+                               int hidden, const __nv_bfloat16 *gain, __nv_bfloat16 *u, float *ss, size_t ss_stride,
+                               cudaStream_t st);
+
+// A tensor map over bf16 [rows, cols] (row-major, 16-byte aligned rows): boxes of 64 columns x box_rows rows with the
+// 128-byte swizzle the tcgen05 operand descriptors expect.
+bool gemm_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows);
 
 // nullptr when the arguments are valid, else the reason.
 const char *gemm_check(const GemmArgs &a);

@@ -968,15 +968,8 @@ template <int BN, int EPI>
 cudaError_t launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int sms,
                       cudaStream_t stream) {
     using C = Cfg<BN>;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!configured[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured[dev & 63] = true;
-    }
+    static SmemOptIn opt;
+    if (cudaError_t e = opt.set((const void *)gemm_kernel<BN, EPI>, C::SMEM_BYTES)) return e;
     int m_tiles = (args.M + BM - 1) / BM, n_tiles = (args.N + BN - 1) / BN;
     int total = m_tiles * n_tiles * args.splits;
     int grid = total < sms ? total : sms;
@@ -987,15 +980,8 @@ cudaError_t launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const GemmAr
 template <int EPI>
 cudaError_t launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int sms,
                         cudaStream_t stream) {
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!configured[dev & 63]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
-        if (e != cudaSuccess) return e;
-        configured[dev & 63] = true;
-    }
+    static SmemOptIn opt;
+    if (cudaError_t e = opt.set((const void *)gemm_pair_kernel<EPI>, kPairSmem)) return e;
     const int total = ((args.M + 255) / 256) * ((args.N + 255) / 256);
     const int pairs = total < sms / 2 ? total : sms / 2;
     return launch_kernel(gemm_pair_kernel<EPI>, dim3(2 * pairs), dim3(kThreads), kPairSmem, stream, ta, tb, args);
@@ -1018,6 +1004,10 @@ cudaError_t launch_epi(const CUtensorMap &ta, const CUtensorMap &tb, const GemmA
 }
 
 }  // namespace
+
+bool gemm_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    return make_tmap_2d(map, ptr, rows, cols, box_rows);
+}
 
 const char *gemm_check(const GemmArgs &a) {
     if (a.M < 1 || a.N < 1 || a.K < 1) return "M, N and K must be positive";

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 
 namespace lrm {
@@ -32,6 +33,27 @@ std::string thread_error();
 // previous kernel writes).
 bool pdl_enabled();
 void set_pdl(bool on);
+
+// A kernel's dynamic shared-memory opt-in, made once per device. The library's entry points may be called from
+// several host threads (one per device, or several on one device), so each call site keeps one of these as a
+// function-local static and the flag is read and set under its lock.
+struct SmemOptIn {
+    std::mutex mu;
+    bool done[64] = {};
+    cudaError_t set(const void *kernel, int bytes) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+        std::lock_guard<std::mutex> g(mu);
+        if (!done[dev]) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+            if (e != cudaSuccess) return e;
+            done[dev] = true;
+        }
+        return cudaSuccess;
+    }
+};
 
 // Launches `kernel` with programmatic stream serialization when pdl_enabled().
 template <typename... KArgs, typename... Args>

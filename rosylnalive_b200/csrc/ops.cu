@@ -10,6 +10,7 @@
 #include "../../include/lrm_cuda.h"
 #include "gemm.h"
 #include "internal.h"
+#include "ptx.cuh"
 #include "qwen.h"
 
 namespace lrm {
@@ -59,6 +60,21 @@ int device_sms() {
     DeviceState *s = device_state();
     return s ? s->sms : 148;
 }
+
+namespace {
+// The bounded wait every kernel of this library uses (ptx::mbar_wait), on an mbarrier that nothing ever arrives on:
+// the wait gives up after `polls` polls, records `code` in the error word and the kernel returns. No copy is issued,
+// so nothing is in flight when it returns.
+__global__ void wait_probe_kernel(uint32_t polls, uint32_t code, uint32_t *err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        ptx::fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ptx::mbar_wait(&bar, 0, err, code, polls);
+}
+}  // namespace
 
 lrm_status op_fail(lrm_status s, const std::string &m) {
     set_thread_error(m);
@@ -152,10 +168,24 @@ lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d
     return op_cuda(launch_prefill_attention_tc(a, d->total_tokens, err, (cudaStream_t)stream), "prefill attention");
 }
 
+// Page counts above 2^20 (16M tokens a sequence) are refused, so split counts and scratch sizes stay far from
+// overflow in every integer type they pass through.
+static constexpr int32_t kMaxDecodePages = 1 << 20;
+
+lrm_status lrm_op_wait_probe(void *stream, uint32_t polls, uint32_t code) {
+    if (polls < 1 || polls > ptx::kWaitLimit) return op_fail(LRM_ERR_ARGUMENT, "wait probe: polls must be 1 .. 2^24");
+    if (code == 0) return op_fail(LRM_ERR_ARGUMENT, "wait probe: the code must be nonzero");
+    uint32_t *err = device_error_word();
+    if (!err) return LRM_ERR_CUDA;
+    wait_probe_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(polls, code, err);
+    return op_cuda(cudaGetLastError(), "wait probe");
+}
+
 uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int32_t pages_per_seq,
                                            int32_t pages_per_split) {
     if (batch < 1 || kv_heads < 1 || pages_per_seq < 1 || pages_per_split < 1) return 0;
-    const uint64_t splits = (pages_per_seq + pages_per_split - 1) / pages_per_split;
+    if (pages_per_seq > kMaxDecodePages || pages_per_split > kMaxDecodePages) return 0;
+    const uint64_t splits = ((uint64_t)pages_per_seq + (uint64_t)pages_per_split - 1) / (uint64_t)pages_per_split;
     const uint64_t states = (uint64_t)batch * kv_heads * splits * 2;
     return states * (128 + 2) * sizeof(float);
 }
@@ -166,6 +196,8 @@ static const char *decode_attn_args(const lrm_decode_attn_desc *d, DecodeAttnArg
     if (d->batch < 1 || d->batch > 65535 || d->kv_heads < 1 || d->kv_heads > 65535 || d->q_heads != 2 * d->kv_heads)
         return "decode attention: bad sizes (q_heads must be 2 * kv_heads)";
     if (d->pages_per_seq < 1 || d->pages_per_split < 1) return "decode attention: page counts must be positive";
+    if (d->pages_per_seq > kMaxDecodePages || d->pages_per_split > kMaxDecodePages)
+        return "decode attention: pages_per_seq and pages_per_split must be at most 2^20";
     if (!d->q || !d->pool || !d->page_table || !d->seq_len || !d->slots || !d->out)
         return "decode attention: null pointer";
     if ((d->q | d->pool | d->out) & 15) return "decode attention: q, pool and out must be 16-byte aligned";
@@ -176,7 +208,7 @@ static const char *decode_attn_args(const lrm_decode_attn_desc *d, DecodeAttnArg
     a.B = d->batch;
     a.q_heads = d->q_heads;
     a.pages_per_split = d->pages_per_split;
-    a.max_splits = (d->pages_per_seq + d->pages_per_split - 1) / d->pages_per_split;
+    a.max_splits = (int32_t)(((int64_t)d->pages_per_seq + d->pages_per_split - 1) / d->pages_per_split);
     a.scale_log2 = d->scale * 1.4426950408889634f;
     a.out = (__nv_bfloat16 *)d->out;
     return nullptr;

@@ -59,9 +59,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for phase `parity` to complete. On timeout, writes `code` to *err (first writer wins) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
+// Bounded wait for phase `parity` to complete. On timeout (after `limit` polls), writes `code` to *err (first writer
+// wins) and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code,
+                                          uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     if (err) atomicCAS(err, 0u, code);
     return false;
@@ -275,6 +277,16 @@ __device__ __forceinline__ uint32_t mapa(const void *p, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
+}
+
+// 16-byte load from a shared::cluster address (this CTA's or another cluster CTA's shared memory, from mapa).
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
 }
 
 // Arrive on an mbarrier given by its shared::cluster address (possibly in another CTA of the cluster).

@@ -70,6 +70,9 @@ struct DecodeAttnArgs {
     __nv_bfloat16 *out;      // [B][q_heads][128]
     uint32_t *err;
 };
+// A row whose seq_len is below 1 or needs more pages than its page-table row (or than max_splits splits hold) is
+// not read: the attention kernel writes kErrDecodeLen into err and the combine writes the row's output as zeros.
+constexpr uint32_t kErrDecodeLen = 0x2010;
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st);
 
 // Causal prefill attention for query rows q [T][q_heads][128] of sequences packed by cu_seqlens; out bf16

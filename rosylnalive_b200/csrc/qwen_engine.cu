@@ -296,6 +296,10 @@ static lrm_status sync_check(lrm_qwen Q) {
     if (code) {
         cudaMemset(Q->err, 0, 4);
         char buf[96];
+        if (code == kErrDecodeLen) {
+            snprintf(buf, sizeof buf, "decode attention: a row's key count exceeds its page table (code 0x%x)", code);
+            return qfail(Q, LRM_ERR_STATE, buf);
+        }
         snprintf(buf, sizeof buf, "a kernel's bounded wait gave up (code 0x%x)", code);
         return qfail(Q, LRM_ERR_TIMEOUT, buf);
     }

@@ -336,6 +336,14 @@ __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, in
 //   values: lane owns dims 4 lane .. 4 lane + 3 (8-byte smem loads), weights broadcast from shared memory.
 // The four warps' states merge in shared memory and the split's (max, sum, unnormalised output) go to part_*; the
 // combine kernel merges the splits.
+// A row's key count is usable when it is at least 1 and its pages fit both the page-table row and the max_splits
+// split states per (row, kv head) that the scratch holds; anything else would read another row's pages or states.
+__device__ __forceinline__ bool decode_len_ok(const DecodeAttnArgs &a, int len) {
+    if (len < 1) return false;
+    const long long npages = ((long long)len + kPageTokens - 1) / kPageTokens;
+    return npages <= a.kv.max_pages_per_seq && npages <= (long long)a.max_splits * a.pages_per_split;
+}
+
 template <int ST>
 __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
     // Consumer warp w takes the pages j = w (mod 4) and page j sits in stage j % ST. With ST a multiple of 4 every
@@ -357,6 +365,10 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int slot = a.slots[b];
     const int len = a.seq_len[slot];
+    if (!decode_len_ok(a, len)) {  // keys beyond the page table: nothing is read, the host sees the code
+        if (split == 0 && h == 0 && threadIdx.x == 0) atomicCAS(a.err, 0u, kErrDecodeLen);
+        return;
+    }
     const int npages = (len + kPageTokens - 1) / kPageTokens;
     const int p0 = split * a.pages_per_split;
     if (p0 >= npages) return;  // whole CTA, before any barrier
@@ -526,6 +538,10 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
     const int b = blockIdx.x, qh = blockIdx.y, d = threadIdx.x;
     const int h = qh / 2, hh = qh % 2;
     const int len = a.seq_len[a.slots[b]];
+    if (!decode_len_ok(a, len)) {  // the attention kernel recorded the error; the row is written as zeros
+        a.out[((size_t)b * a.q_heads + qh) * kHeadDim + d] = __float2bfloat16_rn(0.f);
+        return;
+    }
     const int npages = (len + kPageTokens - 1) / kPageTokens;
     const int nsplit = (npages + a.pages_per_split - 1) / a.pages_per_split;
     const size_t base = ((size_t)b * a.kv.kv_heads + h) * a.max_splits;
@@ -619,17 +635,10 @@ cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
     constexpr int ST = 4;  // 37 KiB of shared memory a CTA, six CTAs an SM (measured faster than 8 / 12 / 16)
     const size_t smem = ST * 8192 + (4 * 32 + 4 * 2 * 128 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!configured[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        configured[dev & 63] = true;
-    }
-    cudaError_t e = launch_kernel(decode_attn_kernel<ST>, dim3(a.max_splits, a.kv.kv_heads, a.B), dim3(160), smem, st,
-                                  a);
+    static SmemOptIn opt;
+    cudaError_t e = opt.set((const void *)decode_attn_kernel<ST>, (int)smem);
+    if (e != cudaSuccess) return e;
+    e = launch_kernel(decode_attn_kernel<ST>, dim3(a.max_splits, a.kv.kv_heads, a.B), dim3(160), smem, st, a);
     if (e != cudaSuccess) return e;
     return launch_kernel(decode_combine_kernel, dim3(a.B, a.q_heads), dim3(128), 0, st, a);
 }

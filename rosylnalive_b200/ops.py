@@ -40,6 +40,7 @@ N.extra_signatures({
     "lrm_op_decode_attention_workspace": [I32, I32, I32, I32],
     "lrm_op_decode_attention": [P, ctypes.POINTER(DecodeAttnDesc)],
     "lrm_op_decode_attention_static": [P, ctypes.POINTER(DecodeAttnDesc)],
+    "lrm_op_wait_probe": [P, U32, U32],
 }, {"lrm_op_decode_attention_workspace": U64})
 
 # Scratch built into liblrmcuda.so for lrm_op_decode_attention_static (LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES).
@@ -61,6 +62,12 @@ def error_word(clear: bool = True) -> int:
     v = ctypes.c_uint32()
     N.check(N.lib().lrm_op_error_word(ctypes.byref(v), 1 if clear else 0), None, "error_word")
     return v.value
+
+
+def wait_probe(polls: int, code: int, stream=None):
+    """Launches a kernel whose bounded wait cannot complete: after `polls` polls it records `code` in the error word
+    and returns (the path every kernel takes when a wait runs out)."""
+    N.check(N.lib().lrm_op_wait_probe(_stream(stream), polls, code), None, "wait_probe")
 
 
 def gemm(a, b, out, epilogue=GEMM_F32, resid=None, splits=1, bn=0, ldo=None, split_stride=0, cta_pair=0,

@@ -61,7 +61,7 @@ def _device():
     assert ops.error_word() == 0
 
 
-@pytest.mark.parametrize("lens", [(2048, 2048), (70, 129, 1, 64)])
+@pytest.mark.parametrize("lens", [(2048,) * 8, (70, 129, 1, 64)])
 def test_prefill_attention(tables, lens):
     cos, sin = tables
     qs, ks, vs = zip(*(make_qkv(L, 100 + i, cos, sin) for i, L in enumerate(lens)))
@@ -126,3 +126,46 @@ def test_decode_attention_rejects_bad_shapes():
     ws = torch.empty(1 << 16, device="cuda")
     with pytest.raises(ValueError):
         ops.decode_attention(q, pool, t, lens, lens, q, ws, 1, 0.1)
+
+
+def test_decode_attention_row_longer_than_its_page_table(tables):
+    # Row 1 claims 113 keys but its page-table row holds 7 pages (112 tokens). Both kernels check every row's key
+    # count against the table before reading it: that row's pages and split states are not touched, the error word
+    # gets 0x2010 and the row's output is zeros; the other rows are computed as usual.
+    cos, sin = tables
+    lens, maxp, pps = (100, 100, 50), 7, 2
+    B = len(lens)
+    pool = np.zeros((B * maxp, KVH, 2, 16, HD), np.float32)
+    table = np.arange(B * maxp, dtype=np.int32).reshape(B, maxp)
+    qrows, refs = [], []
+    for b, L in enumerate(lens):
+        q, k, v = make_qkv(L, 300 + b, cos, sin)
+        for p in range((L + 15) // 16):
+            t0, t1 = 16 * p, min(L, 16 * p + 16)
+            pool[table[b, p], :, 0, :t1 - t0] = k[t0:t1].reshape(t1 - t0, KVH, HD).transpose(1, 0, 2)
+            pool[table[b, p], :, 1, :t1 - t0] = v[t0:t1].reshape(t1 - t0, KVH, HD).transpose(1, 0, 2)
+        qrows.append(q[L - 1])
+        refs.append(O.attention(q[L - 1:L], k, v, QH, KVH, HD, L - 1, SCALE, "f64")[0])
+    dlens = torch.tensor([lens[0], maxp * 16 + 1, lens[2]], dtype=torch.int32, device="cuda")
+    slots = torch.arange(B, dtype=torch.int32, device="cuda")
+    ws = torch.empty(ops.decode_attention_workspace(B, KVH, maxp, pps) // 4, device="cuda")
+    out = torch.full((B, QH, HD), float("nan"), device="cuda", dtype=torch.bfloat16)
+    ops.decode_attention(to_dev(np.stack(qrows), (B, QH, HD)), to_dev(pool, pool.shape),
+                         torch.from_numpy(table).cuda(), dlens, slots, out, ws, pps, SCALE)
+    torch.cuda.synchronize()
+    assert ops.error_word(clear=True) == 0x2010
+    got = out.float().cpu().numpy().reshape(B, QH * HD)
+    assert np.all(got[1] == 0)
+    for b in (0, 2):
+        assert rel(got[b], refs[b]) <= 1e-2, (b, rel(got[b], refs[b]))
+
+
+def test_decode_attention_refuses_page_counts_above_2_20():
+    q = torch.zeros(1, 16, 128, device="cuda", dtype=torch.bfloat16)
+    pool = torch.zeros(1, 8, 2, 16, 128, device="cuda", dtype=torch.bfloat16)
+    t = torch.zeros(1, 1, dtype=torch.int32, device="cuda")
+    lens = torch.ones(1, dtype=torch.int32, device="cuda")
+    assert ops.decode_attention_workspace(1, 8, (1 << 20) + 1, 1) == 0
+    assert ops.decode_attention_workspace(1, 8, 1 << 20, (1 << 20) + 1) == 0
+    with pytest.raises(ValueError):
+        ops.decode_attention(q, pool, t, lens, lens, q, torch.empty(1 << 10, device="cuda"), (1 << 20) + 1, 0.1)

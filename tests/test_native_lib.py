@@ -68,3 +68,14 @@ def test_torch_inv_freq_matches_pins(tiny_golden):
 def test_rope_table_rejects_bad_arguments():
     with pytest.raises(ValueError):
         N.rope_table(np.array([0x7F800000], np.uint32), 4)  # inf
+
+
+def test_device_info_layout_matches_the_raw_binding():
+    # The F# binding passes lrm_device_info as 616 raw bytes and decodes fields at these offsets.
+    import ctypes
+
+    C = N.DeviceInfoC
+    assert ctypes.sizeof(C) == 616
+    want = {"index": 0, "name": 4, "vendor_id": 260, "pci_device_id": 264, "driver": 268, "memory_bytes": 336,
+            "sm_count": 344, "cc_major": 348, "cc_minor": 352, "accepted": 356, "rejection": 360}
+    assert {k: getattr(C, k).offset for k in want} == want
