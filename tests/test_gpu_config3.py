@@ -10,7 +10,12 @@ is compared on the same prefix:
     greedy run keeps the oracle's tokens at least until the first step whose margin does not;
   * the fp32 catalog path (Fp32Executor over the device API): logits within 1e-4 max-abs at every step and the same
     argmax at every step whose oracle margin is above 1e-3.
-The oracle's prefill of 512 tokens plus 127 decode steps at this size takes about half a minute of host CPU."""
+The oracle's prefill of 512 tokens plus 127 decode steps at this size takes about half a minute of host CPU.
+
+The free-running greedy identity over 64 steps is checked on the prompt tests/golden/config3_greedy.py selects the way
+the reference selects its greedy goldens (every step's top-2 margin at least twice the worst bf16 logit error): the
+engine's own greedy run, fed nothing but the prompt, must give the oracle's 64 tokens exactly (from the committed
+fixture tests/golden/config3_greedy.npz), with every step's logits within the same bars as above."""
 
 import dataclasses
 
@@ -30,6 +35,7 @@ if cuda_available():
     from rosylnalive_b200 import synthetic as S
 
 PROMPT, STEPS = 512, 128
+CONFIG3_GREEDY_SHA256 = "6537621ec990b5578e73e439a78a71f9dfeb7966c15b63c2cc5fc9fede03e21a"
 
 
 def top2_margin(logits):
@@ -128,3 +134,30 @@ def test_config3_checkpoint_streams_to_the_same_logits(config3, tmp_path):
         eng.close()
     assert np.array_equal(got, want)
     print(f"checkpoint load incl. engine creation: {load_s:.2f} s for {sum(w.nbytes for w in weights.values()) / 1e9:.2f} GB")
+
+
+def test_config3_bf16_free_running_greedy_64_steps_identical():
+    import hashlib
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "config3_greedy.npz")
+    with open(path, "rb") as f:
+        assert hashlib.sha256(f.read()).hexdigest() == CONFIG3_GREEDY_SHA256
+    fx = dict(np.load(path))
+    cfg = dataclasses.replace(S.QWEN3_0_6B, max_pos=PROMPT + STEPS + 16)
+    weights = S.random_weights(cfg, seed=0)
+    cos, sin = R.t_spec(R.torch_inv_freq_bits(cfg.rope_theta, cfg.head_dim), cfg.max_pos)
+    prompt = S.random_prompt(cfg.vocab, PROMPT, seed=int(fx["seed"]), stream="config3-greedy")
+    steps = len(fx["ids"])
+    assert steps == 64 and fx["margin"].min() >= float(fx["min_margin"])
+    with Qw.QwenEngine(cfg, weights, cos, sin, max_seqs=1, max_tokens=PROMPT, max_batch=1) as eng:
+        ids, logits = eng.greedy([prompt], steps, want_logits=True)
+    assert np.array_equal(ids[0], fx["ids"]), (ids[0], fx["ids"])
+    cols = fx["columns"]
+    for s in range(steps):
+        c = np.concatenate([cols, fx["top_idx"][s]])
+        want = np.concatenate([fx["cols_val"][s], fx["top_val"][s]]).astype(np.float64)
+        got = logits[0, s].astype(np.float64)[c]
+        assert cosine(got, want) >= 0.9999, s
+        assert np.sqrt(np.mean((got - want) ** 2)) <= 5e-3, s
+        assert np.max(np.abs(got - want)) <= 2.5e-2, s
