@@ -27,6 +27,7 @@ SOURCES = [
     "rope_host.cpp",
     "ops.cu",
     "gemm_tcgen05.cu",
+    "gemm_decode.cu",
     "qwen_kernels.cu",
     "flash_tc.cu",
     "qwen_engine.cu",

@@ -75,7 +75,7 @@ __device__ __forceinline__ void norm_rope_pair(float &lo, float &hi, float r, fl
 }
 
 // silu(g) = g / (1 + e^-g) with the approximate division (rcp.approx, about 2 ulp in fp32; the result is rounded to
-// bf16 next), the form the decode path's swiglu_reduce uses too.
+// bf16 next), the form the decode GEMMs' SwiGLU epilogue (gemm_decode.cu) uses too.
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // The epilogue of one accumulator row (thread = TMEM lane): row `row` of the output, columns n0..n0+BN-1, read

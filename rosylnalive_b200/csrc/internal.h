@@ -40,7 +40,8 @@ void set_pdl(bool on);
 struct SmemOptIn {
     std::mutex mu;
     bool done[64] = {};
-    cudaError_t set(const void *kernel, int bytes) {
+    // With big_clusters, the kernel also opts into clusters above the portable 8 CTAs.
+    cudaError_t set(const void *kernel, int bytes, bool big_clusters = false) {
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
@@ -48,6 +49,8 @@ struct SmemOptIn {
         std::lock_guard<std::mutex> g(mu);
         if (!done[dev]) {
             e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+            if (e == cudaSuccess && big_clusters)
+                e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
             if (e != cudaSuccess) return e;
             done[dev] = true;
         }

@@ -25,35 +25,12 @@ __host__ __device__ inline size_t kv_page_elems(int kv_heads) { return (size_t)k
 cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
                               const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st);
 
-// x[t] += sum_s partial[s][t] (splits >= 0; 0 = no add); xn[t] = bf16(rmsnorm(x[t]) * w). With splits > 0 and w
-// null only the sum is written. splits 0 runs the warp-per-row form (prefill); splits > 0 the block-per-row form.
-cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
-                              const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st);
-// xn[t] = bf16(rmsnorm(x[t]) * w) in the block-per-row form of launch_resid_norm, whose sum of squares has the same
-// order as a decode step's fused residual + norm (a pipeline stage resumes a decode step with it).
-cudaError_t launch_norm_rows_block(float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
+// xn[t] = bf16(rmsnorm(x[t]) * w) for the T rows of x (fp32 [T][hidden]): one warp a row (the prefill form).
+cudaError_t launch_norm_rows(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn,
+                             cudaStream_t st);
+// The same in the block-per-row form (the decode step's final norm).
+cudaError_t launch_norm_rows_block(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
                                    __nv_bfloat16 *xn, cudaStream_t st);
-
-// From qkv = sum_s partial[s] ([T][q+2kv heads][128] fp32): q = rope(rmsnorm(q_head) * q_norm) -> q_out bf16,
-// k = rope(rmsnorm(k_head) * k_norm) and raw v -> bf16 into the paged cache at (tok_slot[t], tok_pos[t]) and, when
-// k_out/v_out are given, into contiguous [T][kv][128] copies.
-struct QkvArgs {
-    const float *qkv;
-    int splits;
-    size_t split_stride;
-    int T, q_heads, kv_heads;
-    const __nv_bfloat16 *q_norm, *k_norm;
-    float eps;
-    const float *cos_t, *sin_t;  // [max_pos][64]
-    const int32_t *tok_slot, *tok_pos;
-    KvLayout kv;
-    __nv_bfloat16 *q_out, *k_out, *v_out;
-};
-cudaError_t launch_qk_norm_rope_kv(const QkvArgs &a, cudaStream_t st);
-
-// act[t][j] = bf16(silu(g) * u) with g, u = sum_s partial[s][t] over the 64-interleaved gate/up columns.
-cudaError_t launch_swiglu_reduce(const float *partial, int splits, size_t split_stride, int T, int inter,
-                                 __nv_bfloat16 *act, cudaStream_t st);
 
 // Paged split-K decode attention: one query per sequence (row b, slot slots[b], seq_len[slot] keys including the new
 // one), GQA group 2, pages_per_split pages per CTA; then the combine writes out bf16 [B][q_heads][128].

@@ -5,20 +5,23 @@
 // final norm; tied lm_head; argmax) from the fused kernels:
 //
 //   prefill (T tokens of packed sequences)            decode step (B rows, one token each)
-//   embed_norm                                        advance (positions, lengths) ; embed_norm
+//   embed_norm                                        advance (positions, lengths) ; decode_prep (embed; norm inputs)
 //   per layer:                                        per layer:
-//     GEMM xn.Wqkv^T -> qkv fp32                        GEMM Wqkv.xn^T split-K -> partials
-//     (q/k/v epilogue: q; k, v into the paged cache)    qk_norm_rope_kv (reduces the splits)
-//     flash prefill attention over the cache -> attn    paged split-K decode attention + combine
-//     GEMM attn.Wo^T, epilogue x += .                   GEMM Wo.attn^T split-K ; resid_norm (x += sum; norm)
-//     resid_norm (post norm) -> xn                      GEMM Wgu.xn^T split-K ; swiglu_reduce
-//     GEMM xn.Wgu^T, SwiGLU epilogue -> act             GEMM Wdown.act^T split-K ; resid_norm (next norm)
+//     GEMM xn.Wqkv^T -> qkv fp32                        GEMM Wqkv.u^T + norm scale, QK-norm, RoPE, KV append
+//     (q/k/v epilogue: q; k, v into the paged cache)    paged split-K decode attention + combine
+//     flash prefill attention over the cache -> attn    GEMM Wo.attn^T + x += . ; next norm's inputs
+//     GEMM attn.Wo^T, epilogue x += .                   GEMM Wgu.u^T + norm scale, SwiGLU
+//     resid_norm (post norm) -> xn                      GEMM Wdown.act^T + x += . ; next norm's inputs
+//     GEMM xn.Wgu^T, SwiGLU epilogue -> act
 //     GEMM act.Wdown^T, epilogue x += . ; resid_norm
-//   gather last rows ; lm_head GEMM ; argmax          lm_head GEMM ; argmax
+//   gather last rows ; lm_head GEMM ; argmax          final norm ; lm_head GEMM ; argmax
 //
-// Decode GEMMs swap A and B (weights fill the 128-row tensor-core tile, the B <= 64 tokens are N) and split K so
-// every weight matrix is streamed by ~128 CTAs; the consumers reduce the splits in a fixed order. The decode step is
-// a fixed sequence of launches over device-resident inputs, so it is captured once as a CUDA graph and replayed.
+// Decode GEMMs swap A and B (weights fill the 128-row tensor-core tile, the B <= 64 tokens are N) and split K over a
+// cluster of CTAs that reduces through distributed shared memory and runs the consumer itself (gemm_decode.cu). A
+// token's RMSNorm is applied as a scale of the next GEMM's output rows: the GEMM reads u = bf16(gain * x) and the
+// per-128-column sums of squares of x, which the producing GEMM writes, so no kernel boundary waits for a whole
+// row's norm. The decode step is a fixed sequence of launches over device-resident inputs, so it is captured once as
+// a CUDA graph and replayed.
 //
 // A pipeline stage (lrm_qwen_create_stage) holds layers [first, end) of the model and their KV cache: the first
 // stage embeds ids, the last applies the final norm and the tied head; between stages the fp32 residual x crosses
@@ -93,6 +96,8 @@ struct lrm_qwen_s {
     int32_t *tok_slot = nullptr, *tok_pos = nullptr, *cu = nullptr, *last_idx = nullptr, *d_slots = nullptr;
     int32_t *pf_slot = nullptr, *pf_past = nullptr;  // per prefill sequence: its slot and cached tokens before it
     float *x = nullptr, *qkv = nullptr, *partial = nullptr, *part_o = nullptr, *part_ml = nullptr;
+    float *ss = nullptr;  // decode: per-128-column sums of squares of x [hidden / 128][ss_stride], the norm inputs
+    size_t ss_stride = 0;
     __nv_bfloat16 *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xl = nullptr;
     size_t partial_elems = 0;
     int max_splits_attn = 0;
@@ -129,24 +134,6 @@ static lrm_status qcuda(lrm_qwen q, cudaError_t e, const char *what) {
         cudaError_t e_ = (call);                         \
         if (e_ != cudaSuccess) return qcuda(q, e_, what); \
     } while (0)
-
-// Split counts for the decode GEMMs: the fewest k-blocks on the busiest SM. A launch runs min(tiles, sms) CTAs that
-// take the m_tiles x s tiles round robin, so s splits cost waves(m_tiles * s) x ceil(kb / s) k-blocks; ties go to
-// fewer splits (fewer partials for the consumer to reduce). No split may be empty.
-static int choose_splits(int m_tiles, int kb, int sms) {
-    int best = 1;
-    long best_cost = -1;
-    for (int s = 1; s <= kb; ++s) {
-        const int per = (kb + s - 1) / s;
-        if (per * (s - 1) >= kb) continue;  // the last split would be empty
-        const long cost = (((long)m_tiles * s + sms - 1) / sms) * per;
-        if (best_cost < 0 || cost < best_cost) {
-            best_cost = cost;
-            best = s;
-        }
-    }
-    return best;
-}
 
 static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, int K, int epi, int bn, int splits,
                        void *out, int ldo, const float *resid, int ldr, size_t split_stride,
@@ -186,6 +173,22 @@ static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, i
     return qcuda(Q, gemm_launch(a, Q->sms, Q->stream), "gemm");
 }
 
+// A decode-step GEMM with its consumer fused (gemm_decode.cu): W [M, K] times the step's B tokens [B, K].
+static lrm_status dgemm(lrm_qwen Q, DecodeGemmArgs &a, int epi, const void *W, const void *Bop, int M, int K, int B) {
+    a.M = M;
+    a.N = B;
+    a.K = K;
+    a.A = W;
+    a.B = Bop;
+    a.epi = epi;
+    a.splits = decode_gemm_splits(M, K, Q->sms);
+    const int nkb = (K + 63) / 64;
+    a.kb_per_split = (nkb + a.splits - 1) / a.splits;
+    a.err = Q->err;
+    if (const char *why = decode_gemm_check(a)) return qfail(Q, LRM_ERR_ARGUMENT, std::string("decode gemm: ") + why);
+    return qcuda(Q, decode_gemm_launch(a, Q->stream), "decode gemm");
+}
+
 #define LTRY(expr)                      \
     do {                                \
         lrm_status s_ = (expr);         \
@@ -214,41 +217,40 @@ static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
     const int nqkv = Q->qkv_rows;
     KTRY(Q, launch_advance(Q->d_slots, B, Q->d_seq_len, Q->tok_pos, st), "advance");
-    if (Q->is_first)
-        KTRY(Q, launch_embed_norm(Q->ids, B, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
-             "embed_norm");
-    else  // x[0, B) holds the previous stage's residual
-        KTRY(Q, launch_norm_rows_block(Q->x, B, H, Q->layers[0].in_norm, c.eps, Q->xn, st), "norm");
-    const int s_qkv = choose_splits((nqkv + 127) / 128, (H + 63) / 64, Q->sms);
-    const int s_o = choose_splits((H + 127) / 128, (qh * kHeadDim + 63) / 64, Q->sms);
-    const int s_gu = choose_splits((2 * I + 127) / 128, (H + 63) / 64, Q->sms);
-    const int s_d = choose_splits((H + 127) / 128, (I + 63) / 64, Q->sms);
+    // The first layer's norm inputs: u = bf16(in_norm * x) (in xn) and the per-128-column sums of squares of x.
+    // x[0, B) is the embedding of the ids on the first stage, the previous stage's residual on the others.
+    KTRY(Q, launch_decode_prep(Q->is_first ? Q->ids : nullptr, Q->embed, c.vocab, Q->x, B, H, Q->layers[0].in_norm,
+                               Q->xn, Q->ss, Q->ss_stride, st),
+         "decode prep");
+    DecodeGemmArgs base;
+    memset(&base, 0, sizeof base);
     for (int l = 0; l < Q->nl; ++l) {
         const Layer &L = Q->layers[l];
-        LTRY(gemm(Q, L.w_qkv, Q->xn, nqkv, B, H, EPI_PARTIAL, 64, s_qkv, Q->partial, nqkv, nullptr, 0,
-                  (size_t)B * nqkv));
-        QkvArgs qa;
-        qa.qkv = Q->partial;
-        qa.splits = s_qkv;
-        qa.split_stride = (size_t)B * nqkv;
-        qa.T = B;
-        qa.q_heads = qh;
-        qa.kv_heads = kvh;
-        qa.q_norm = L.q_norm;
-        qa.k_norm = L.k_norm;
+        // q/k/v with the input norm's scale, QK-norm, RoPE and the paged KV append
+        DecodeGemmArgs qa = base;
+        qa.ss = Q->ss;
+        qa.nss = H / 128;
+        qa.hidden = H;
+        qa.ss_stride = Q->ss_stride;
         qa.eps = c.eps;
-        qa.cos_t = Q->cos_t;
-        qa.sin_t = Q->sin_t;
-        qa.tok_slot = Q->d_slots;
-        qa.tok_pos = Q->tok_pos;
-        qa.kv = KvLayout{Q->pool + (size_t)l * Q->layer_pool_elems, Q->d_pages, Q->maxp, kvh};
-        qa.q_out = Q->q;
-        qa.k_out = nullptr;
-        qa.v_out = nullptr;
-        KTRY(Q, launch_qk_norm_rope_kv(qa, st), "qk_norm_rope_kv");
+        QkvEpilogue &qe = qa.qkv;
+        qe.q_out = Q->q;
+        qe.pool = Q->pool + (size_t)l * Q->layer_pool_elems;
+        qe.pages = Q->d_pages;
+        qe.pages_per_seq = Q->maxp;
+        qe.q_heads = qh;
+        qe.kv_heads = kvh;
+        qe.q_norm = L.q_norm;
+        qe.k_norm = L.k_norm;
+        qe.eps = c.eps;
+        qe.cos_t = Q->cos_t;
+        qe.sin_t = Q->sin_t;
+        qe.tok_slot = Q->d_slots;
+        qe.tok_pos = Q->tok_pos;
+        LTRY(dgemm(Q, qa, DEC_QKV, L.w_qkv, Q->xn, nqkv, H, B));
         DecodeAttnArgs da;
         da.q = Q->q;
-        da.kv = qa.kv;
+        da.kv = KvLayout{qe.pool, Q->d_pages, Q->maxp, kvh};
         da.slots = Q->d_slots;
         da.seq_len = Q->d_seq_len;
         da.B = B;
@@ -263,19 +265,35 @@ static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
         if (timed) KTRY(Q, cudaEventRecordWithFlags(Q->attn_ev[2 * l], st, cudaEventRecordExternal), "event");
         KTRY(Q, launch_decode_attention(da, st), "decode_attention");
         if (timed) KTRY(Q, cudaEventRecordWithFlags(Q->attn_ev[2 * l + 1], st, cudaEventRecordExternal), "event");
-        LTRY(gemm(Q, L.w_o, Q->attn, H, B, qh * kHeadDim, EPI_PARTIAL, 64, s_o, Q->partial, H, nullptr, 0,
-                  (size_t)B * H));
-        KTRY(Q, launch_resid_norm(Q->x, Q->partial, s_o, (size_t)B * H, B, H, L.post_norm, c.eps, Q->xn, st),
-             "resid_norm");
-        LTRY(gemm(Q, L.w_gu, Q->xn, 2 * I, B, H, EPI_PARTIAL, 64, s_gu, Q->partial, 2 * I, nullptr, 0,
-                  (size_t)B * 2 * I));
-        KTRY(Q, launch_swiglu_reduce(Q->partial, s_gu, (size_t)B * 2 * I, B, I, Q->act, st), "swiglu_reduce");
-        LTRY(gemm(Q, L.w_down, Q->act, H, B, I, EPI_PARTIAL, 64, s_d, Q->partial, H, nullptr, 0, (size_t)B * H));
-        const __nv_bfloat16 *next_norm = next_norm_of(Q, l);  // null: the stage ends with the residual
-        KTRY(Q, launch_resid_norm(Q->x, Q->partial, s_d, (size_t)B * H, B, H, next_norm, c.eps, Q->xn, st),
-             "resid_norm");
+        // o_proj: x += attn Wo^T, then the post-attention norm's inputs
+        DecodeGemmArgs oa = base;
+        oa.x = Q->x;
+        oa.gain = L.post_norm;
+        oa.u = Q->xn;
+        oa.ss_out = Q->ss;
+        oa.ss_stride = Q->ss_stride;
+        LTRY(dgemm(Q, oa, DEC_RESID, L.w_o, Q->attn, H, qh * kHeadDim, B));
+        // gate/up with the post norm's scale and SwiGLU
+        DecodeGemmArgs ga = base;
+        ga.ss = Q->ss;
+        ga.nss = H / 128;
+        ga.hidden = H;
+        ga.ss_stride = Q->ss_stride;
+        ga.eps = c.eps;
+        ga.act = Q->act;
+        ga.ld_act = I;
+        LTRY(dgemm(Q, ga, DEC_SWIGLU, L.w_gu, Q->xn, 2 * I, H, B));
+        // down: x += act Wdown^T, then the next layer's norm inputs (none after a stage's or the model's last layer)
+        DecodeGemmArgs dn = base;
+        dn.x = Q->x;
+        dn.gain = l + 1 < Q->nl ? Q->layers[l + 1].in_norm : nullptr;
+        dn.u = Q->xn;
+        dn.ss_out = Q->ss;
+        dn.ss_stride = Q->ss_stride;
+        LTRY(dgemm(Q, dn, DEC_RESID, L.w_down, Q->act, H, I, B));
     }
     if (!Q->is_last) return LRM_OK;
+    KTRY(Q, launch_norm_rows_block(Q->x, B, H, Q->final_norm, c.eps, Q->xn, st), "final norm");
     LTRY(gemm(Q, Q->embed, Q->xn, c.vocab, B, H, EPI_PARTIAL, 64, 1, Q->partial, c.vocab, nullptr, 0,
               (size_t)B * c.vocab));
     KTRY(Q, launch_argmax(Q->partial, B, c.vocab, Q->next, st), "argmax");
@@ -402,6 +420,7 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     abytes += (size_t)T * H * 4 + (size_t)T * Q->qkv_rows * 4 + part * 4;
     abytes += (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * (128 + 2) * 4;
     abytes += (size_t)T * (H + qh * kHeadDim * 2 + I) * 2 + (size_t)R * H * 2;
+    abytes += (size_t)(H / 128) * R * 4;
     abytes += 64 * 256;
     QTRY(Q.get(), cudaMalloc(&Q->amem, abytes), "activations");
     p = Q->amem;
@@ -424,6 +443,8 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     Q->attn = carve<__nv_bfloat16>(p, (size_t)T * qh * kHeadDim);
     Q->act = carve<__nv_bfloat16>(p, (size_t)T * I);
     Q->xl = carve<__nv_bfloat16>(p, (size_t)R * H);
+    Q->ss_stride = (size_t)R;
+    Q->ss = carve<float>(p, (size_t)(H / 128) * R);
     if ((size_t)(p - Q->amem) > abytes) return qfail(Q.get(), LRM_ERR_STATE, "activation plan overflow");
     QTRY(Q.get(), cudaMallocHost(&Q->h_pinned, sizeof(uint32_t) * (size_t)T * 4), "pinned staging");
     *out = Q.release();
@@ -704,7 +725,7 @@ static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, co
         KTRY(Q, launch_embed_norm(Q->ids, T, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
              "embed_norm");
     else  // x[0, T) holds the previous stage's residual
-        KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, Q->layers[0].in_norm, c.eps, Q->xn, st), "norm");
+        KTRY(Q, launch_norm_rows(Q->x, T, H, Q->layers[0].in_norm, c.eps, Q->xn, st), "norm");
     for (int l = 0; l < Q->nl; ++l) {
         const Layer &L = Q->layers[l];
         // q/k/v GEMM with QK-RMSNorm, RoPE and the paged KV append in its epilogue (no fp32 q/k/v round trip).
@@ -742,11 +763,11 @@ static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, co
         pa.kv_pages = c.kv_pages;
         KTRY(Q, launch_prefill_attention_tc(pa, T, Q->err, st), "prefill_attention");
         LTRY(gemm(Q, Q->attn, L.w_o, T, H, qh * kHeadDim, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
-        KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, L.post_norm, c.eps, Q->xn, st), "resid_norm");
+        KTRY(Q, launch_norm_rows(Q->x, T, H, L.post_norm, c.eps, Q->xn, st), "norm");
         LTRY(gemm(Q, Q->xn, L.w_gu, T, 2 * I, H, EPI_SWIGLU, 256, 1, Q->act, I, nullptr, 0, 0));
         LTRY(gemm(Q, Q->act, L.w_down, T, H, I, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
         if (const __nv_bfloat16 *next_norm = next_norm_of(Q, l))
-            KTRY(Q, launch_resid_norm(Q->x, nullptr, 0, 0, T, H, next_norm, c.eps, Q->xn, st), "resid_norm");
+            KTRY(Q, launch_norm_rows(Q->x, T, H, next_norm, c.eps, Q->xn, st), "norm");
     }
     if (!Q->is_last) return sync_check(Q);
     KTRY(Q, launch_gather_rows(Q->xn, Q->last_idx, nseq, H, Q->xl, st), "gather");

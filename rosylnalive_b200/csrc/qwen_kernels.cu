@@ -3,11 +3,11 @@
 // The reference computes these as separate catalog dispatches (embed_gather_bf16, rmsnorm_rows, rope_apply,
 // copy_rows, silu_mul, add, argmax_rows: src/Lrm.Shaders/hlsl/kernels/basic/*.hlsl). Here each neighbourhood is one
 // kernel so an activation makes one trip through HBM:
-//   embed_norm        embed gather + layer 0's input RMSNorm
-//   resid_norm        split-K reduce of o_proj/down + residual add + the next RMSNorm (decode)
-//   qk_norm_rope_kv   split-K reduce of q/k/v + per-head QK-RMSNorm + RoPE (T_spec table) + paged KV append
-//   swiglu_reduce     split-K reduce of gate/up + SwiGLU (decode)
-// and decode attention streams the paged bf16 KV cache with bulk async copies (see decode_attn_kernel).
+//   embed_norm        embed gather + layer 0's input RMSNorm (prefill)
+//   norm_rows_*       RMSNorm rows (prefill: a warp a row; the decode step's final norm: a block a row)
+//   argmax, gather_rows, advance
+// and decode attention streams the paged bf16 KV cache with bulk async copies (see decode_attn_kernel). The decode
+// step's split-K reductions, residual adds, QK-norm/RoPE/KV append and SwiGLU run inside its GEMMs (gemm_decode.cu).
 #include <cuda_bf16.h>
 #include <math.h>
 #include <stdint.h>
@@ -69,48 +69,23 @@ __global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t *ids, co
         xn[(size_t)t * hidden + c] = __float2bfloat16_rn(x[(size_t)t * hidden + c] * r * bf(w[c]));
 }
 
-// ---- residual + split reduce + norm --------------------------------------------------------------------------------
+// ---- RMSNorm rows ----------------------------------------------------------------------------------------------
 
-// One block per row, 4 consecutive columns per thread (hidden % 4 == 0). The split partials are added in split
-// order, but their loads are issued 8 at a time so a 16-way split costs about two memory latencies, not sixteen.
-__global__ void __launch_bounds__(256) resid_norm_kernel(float *x, const float *partial, int splits,
-                                                         size_t split_stride, int hidden, const __nv_bfloat16 *w,
-                                                         float eps, __nv_bfloat16 *xn) {
+// One block per row, 4 consecutive columns per thread (hidden % 4 == 0): xn = bf16(rmsnorm(x) * w). The decode step's
+// final norm (before the lm_head) and a pipeline stage resuming a decode step use this form.
+__global__ void __launch_bounds__(256) norm_rows_block_kernel(const float *x, int hidden, const __nv_bfloat16 *w,
+                                                              float eps, __nv_bfloat16 *xn) {
     ptx::griddep_wait();
     ptx::griddep_launch();
     __shared__ float red[8];
     const int t = blockIdx.x;
-    float4 *xr = reinterpret_cast<float4 *>(x + (size_t)t * hidden);
-    const float4 *pr = reinterpret_cast<const float4 *>(partial + (size_t)t * hidden);
-    const size_t stride4 = split_stride / 4;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)t * hidden);
     const int n4 = hidden / 4;
     float ss = 0.f;
     for (int c = threadIdx.x; c < n4; c += 256) {
-        float4 v = xr[c];
-        int s = 0;
-        for (; s + 8 <= splits; s += 8) {
-            float4 q[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) q[j] = pr[(s + j) * stride4 + c];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                v.x += q[j].x;
-                v.y += q[j].y;
-                v.z += q[j].z;
-                v.w += q[j].w;
-            }
-        }
-        for (; s < splits; ++s) {
-            const float4 q = pr[s * stride4 + c];
-            v.x += q.x;
-            v.y += q.y;
-            v.z += q.z;
-            v.w += q.w;
-        }
-        if (splits) xr[c] = v;
+        const float4 v = xr[c];
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
-    if (!w) return;  // the residual sum alone (the last layer of a pipeline stage)
     const float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
     for (int c = threadIdx.x; c < n4; c += 256) {
         const float4 v = xr[c];
@@ -173,81 +148,6 @@ __global__ void __launch_bounds__(256) norm_rows_warp_fixed_kernel(const float *
             pack4(v[i].x * r * __uint_as_float(wv.x << 16), v[i].y * r * __uint_as_float(wv.x & 0xFFFF0000u),
                   v[i].z * r * __uint_as_float(wv.y << 16), v[i].w * r * __uint_as_float(wv.y & 0xFFFF0000u));
     }
-}
-
-// ---- q/k norm + RoPE + KV append --------------------------------------------------------------------------------
-
-// One warp per (token, head row); lane l owns dims 4l..4l+3. Head rows 0..q-1 are q, then kv k rows, then kv v rows.
-__global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(QkvArgs a) {
-    ptx::griddep_wait();
-    ptx::griddep_launch();
-    const int warp_global = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int rows = a.q_heads + 2 * a.kv_heads;
-    const int t = warp_global / rows, hr = warp_global % rows;
-    if (t >= a.T) return;
-    const int width = rows * kHeadDim;
-    float4 v = make_float4(0, 0, 0, 0);
-    for (int s = 0; s < a.splits; ++s) {
-        float4 p = *reinterpret_cast<const float4 *>(a.qkv + s * a.split_stride + (size_t)t * width + hr * kHeadDim +
-                                                     4 * lane);
-        v.x += p.x;
-        v.y += p.y;
-        v.z += p.z;
-        v.w += p.w;
-    }
-    const int pos = a.tok_pos[t];
-    const bool is_q = hr < a.q_heads, is_k = !is_q && hr < a.q_heads + a.kv_heads;
-    if (is_q || is_k) {
-        const __nv_bfloat16 *nw = is_q ? a.q_norm : a.k_norm;
-        float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-        float r = rsqrtf(ss / kHeadDim + a.eps);
-        const int d = 4 * lane;
-        float y0 = v.x * r * bf(nw[d]), y1 = v.y * r * bf(nw[d + 1]), y2 = v.z * r * bf(nw[d + 2]),
-              y3 = v.w * r * bf(nw[d + 3]);
-        // NeoX rotate-half: dim i pairs with i + 64, held by lane l ^ 16.
-        float o0 = __shfl_xor_sync(FULL, y0, 16), o1 = __shfl_xor_sync(FULL, y1, 16),
-              o2 = __shfl_xor_sync(FULL, y2, 16), o3 = __shfl_xor_sync(FULL, y3, 16);
-        const int i = 4 * (lane & 15);
-        float4 c = *reinterpret_cast<const float4 *>(a.cos_t + (size_t)pos * 64 + i);
-        float4 s = *reinterpret_cast<const float4 *>(a.sin_t + (size_t)pos * 64 + i);
-        if (lane < 16) {  // y[i] = x[i] c - x[i+64] s
-            v = make_float4(y0 * c.x - o0 * s.x, y1 * c.y - o1 * s.y, y2 * c.z - o2 * s.z, y3 * c.w - o3 * s.w);
-        } else {  // y[i+64] = x[i+64] c + x[i] s
-            v = make_float4(y0 * c.x + o0 * s.x, y1 * c.y + o1 * s.y, y2 * c.z + o2 * s.z, y3 * c.w + o3 * s.w);
-        }
-    }
-    const uint2 packed = pack4(v.x, v.y, v.z, v.w);
-    if (is_q) {
-        *reinterpret_cast<uint2 *>(a.q_out + ((size_t)t * a.q_heads + hr) * kHeadDim + 4 * lane) = packed;
-        return;
-    }
-    const int kvh = is_k ? hr - a.q_heads : hr - a.q_heads - a.kv_heads;
-    const int slot = a.tok_slot[t];
-    const int page = a.kv.pages[(size_t)slot * a.kv.max_pages_per_seq + pos / kPageTokens];
-    __nv_bfloat16 *dst = a.kv.pool + (size_t)page * kv_page_elems(a.kv_heads) +
-                         ((size_t)(kvh * 2 + (is_k ? 0 : 1)) * kPageTokens + pos % kPageTokens) * kHeadDim + 4 * lane;
-    *reinterpret_cast<uint2 *>(dst) = packed;
-    __nv_bfloat16 *contig = is_k ? a.k_out : a.v_out;
-    if (contig) *reinterpret_cast<uint2 *>(contig + ((size_t)t * a.kv_heads + kvh) * kHeadDim + 4 * lane) = packed;
-}
-
-// ---- SwiGLU reduce (decode) ------------------------------------------------------------------------------------
-
-__global__ void swiglu_reduce_kernel(const float *partial, int splits, size_t split_stride, int T, int inter,
-                                     __nv_bfloat16 *act) {
-    ptx::griddep_wait();
-    ptx::griddep_launch();
-    size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= (size_t)T * inter) return;
-    int t = (int)(e / inter), j = (int)(e % inter);
-    size_t base = (size_t)t * (2 * inter) + (j / 64) * 128 + (j % 64);
-    float g = 0.f, u = 0.f;
-    for (int s = 0; s < splits; ++s) {
-        g += partial[s * split_stride + base];
-        u += partial[s * split_stride + base + 64];
-    }
-    act[e] = __float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * u);  // as the prefill GEMM's SwiGLU epilogue
 }
 
 // ---- argmax -------------------------------------------------------------------------------------------------
@@ -588,35 +488,16 @@ cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *e
     return launch_kernel(embed_norm_kernel, dim3(T), dim3(256), 0, st, ids, embed, hidden, vocab, w, eps, x, xn);
 }
 
-cudaError_t launch_resid_norm(float *x, const float *partial, int splits, size_t split_stride, int T, int hidden,
-                              const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn, cudaStream_t st) {
-    if (splits == 0) {
-        if (hidden == 1024)  // Qwen3-0.6B
-            return launch_kernel(norm_rows_warp_fixed_kernel<256>, dim3((T + 7) / 8), dim3(256), 0, st,
-                                 (const float *)x, T, w, eps, xn);
-        return launch_kernel(norm_rows_warp_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float *)x, T, hidden,
-                             w, eps, xn);
-    }
-    return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, partial, splits, split_stride, hidden, w,
-                         eps, xn);
+cudaError_t launch_norm_rows(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn,
+                             cudaStream_t st) {
+    if (hidden == 1024)  // Qwen3-0.6B
+        return launch_kernel(norm_rows_warp_fixed_kernel<256>, dim3((T + 7) / 8), dim3(256), 0, st, x, T, w, eps, xn);
+    return launch_kernel(norm_rows_warp_kernel, dim3((T + 7) / 8), dim3(256), 0, st, x, T, hidden, w, eps, xn);
 }
 
-cudaError_t launch_norm_rows_block(float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
-                                  __nv_bfloat16 *xn, cudaStream_t st) {
-    return launch_kernel(resid_norm_kernel, dim3(T), dim3(256), 0, st, x, (const float *)nullptr, 0, (size_t)0,
-                         hidden, w, eps, xn);
-}
-
-cudaError_t launch_qk_norm_rope_kv(const QkvArgs &a, cudaStream_t st) {
-    const int warps = a.T * (a.q_heads + 2 * a.kv_heads);
-    return launch_kernel(qk_norm_rope_kv_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, a);
-}
-
-cudaError_t launch_swiglu_reduce(const float *partial, int splits, size_t split_stride, int T, int inter,
-                                 __nv_bfloat16 *act, cudaStream_t st) {
-    size_t n = (size_t)T * inter;
-    return launch_kernel(swiglu_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, partial, splits,
-                         split_stride, T, inter, act);
+cudaError_t launch_norm_rows_block(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
+                                   __nv_bfloat16 *xn, cudaStream_t st) {
+    return launch_kernel(norm_rows_block_kernel, dim3(T), dim3(256), 0, st, x, hidden, w, eps, xn);
 }
 
 cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st) {
