@@ -50,6 +50,20 @@ struct GemmArgs {
     // 0 chooses; 1 one CTA per 128 x bn tile; 2 pairs of CTAs (a cluster of two SMs) sharing 256 x 256 tiles through
     // tcgen05 cta_group::2 MMAs (bn 256, one split, not EPI_PARTIAL).
     int cta_pair;
+    // RMSNorm fused into the prefill GEMMs (CTA pairs only). A residual GEMM (EPI_RESID) with norm_u also writes the
+    // next norm's inputs: u[m][n] = bf16(norm_gain[n] * out[m][n]) (row stride ldo) and, per row and 256-column
+    // tile, the sum of squares of out (norm_ss[n / 256][m], row stride norm_ss_stride; the order of
+    // pair_prep_kernel). A consumer (EPI_SWIGLU, EPI_QKV) with row_ss reads such u as A and multiplies each output
+    // row by r[m] = 1 / sqrt(sum_g row_ss[g][m] / row_hidden + row_eps), groups in order: the norm's scale, which
+    // the GEMM, linear in each row, may apply afterwards.
+    const __nv_bfloat16 *norm_gain;
+    __nv_bfloat16 *norm_u;
+    float *norm_ss;
+    size_t norm_ss_stride;
+    const float *row_ss;
+    int row_nss, row_hidden;
+    size_t row_ss_stride;
+    float row_eps;
 };
 
 // ---- decode GEMMs with their consumers fused (gemm_decode.cu) ----------------------------------------------------
@@ -102,6 +116,11 @@ int decode_gemm_splits(int M, int K, int sms);
 cudaError_t launch_decode_prep(const uint32_t *ids, const __nv_bfloat16 *embed, int vocab, float *x, int T,
                                int hidden, const __nv_bfloat16 *gain, __nv_bfloat16 *u, float *ss, size_t ss_stride,
                                cudaStream_t st);
+
+// The prefill norm inputs from the residual stream in the order a residual GEMM with norm_u writes them (a pipeline
+// stage that resumes a prefill): u[t] = bf16(gain * x[t]) and ss[g][t] per 256-column group g.
+cudaError_t launch_pair_prep(const float *x, int T, int hidden, const __nv_bfloat16 *gain, __nv_bfloat16 *u, float *ss,
+                             size_t ss_stride, cudaStream_t st);
 
 // A tensor map over bf16 [rows, cols] (row-major, 16-byte aligned rows): boxes of 64 columns x box_rows rows with the
 // 128-byte swizzle the tcgen05 operand descriptors expect.

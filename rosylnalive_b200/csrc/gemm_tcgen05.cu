@@ -500,6 +500,30 @@ __device__ __forceinline__ void store_bf16_tail(__nv_bfloat16 *dst, uint4 v, int
     }
 }
 
+// One pass's share of a row's sum of squares in the staged epilogue: the lane's four columns (fused multiply-adds in
+// order), then a butterfly over the eight lanes that hold the row's 32 columns of the pass (lanes 8 rq .. 8 rq + 7),
+// which leaves the same bits in all eight. A row's 256-column total adds the eight passes in order. pair_prep_kernel
+// computes the same sums from the residual stream in the same order.
+__device__ __forceinline__ float pair_group_ss(float4 f) {
+    float p = f.x * f.x;
+    p = fmaf(f.y, f.y, p);
+    p = fmaf(f.z, f.z, p);
+    p = fmaf(f.w, f.w, p);
+    p += __shfl_xor_sync(0xffffffffu, p, 1);
+    p += __shfl_xor_sync(0xffffffffu, p, 2);
+    p += __shfl_xor_sync(0xffffffffu, p, 4);
+    return p;
+}
+
+// The RMSNorm scale of output row m for a consumer GEMM whose A rows are bf16(gain * x): the row's group sums added
+// in group order (1 for a row past M, or without row_ss).
+__device__ __forceinline__ float row_norm_scale(const GemmArgs &args, int m) {
+    if (!args.row_ss || m >= args.M) return 1.f;
+    float s = 0.f;
+    for (int g = 0; g < args.row_nss; ++g) s += args.row_ss[(size_t)g * args.row_ss_stride + m];
+    return rsqrtf(s / args.row_hidden + args.row_eps);
+}
+
 // One warp's share of a 256 x 256 pair tile: output rows row0..row0+31 (TMEM lanes of t_warp), columns n0..n0+255.
 // buf: the warp's two staging buffers (shared::cta addresses).
 template <int EPI>
@@ -507,6 +531,12 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
                                                 uint32_t buf, int lane) {
     const int sub = lane & 7, rq = lane >> 3;  // read-back: 16-byte chunk, row within each group of four
     if (EPI == EPI_F32 || EPI == EPI_RESID) {
+        // With the fused norm (EPI_RESID and norm_u): the row's sum of squares over this 256-column tile, one entry
+        // per row the lane writes (rows 4 it + rq); see pair_group_ss.
+        const bool fused_norm = EPI == EPI_RESID && args.norm_u != nullptr;
+        float ssacc[8];
+#pragma unroll
+        for (int it = 0; it < 8; ++it) ssacc[it] = 0.f;
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {  // 32 fp32 columns a pass
             const uint32_t b = buf + (c & 1) * kStageBuf;
@@ -528,27 +558,54 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
                         res[it] = *reinterpret_cast<const float4 *>(args.resid + (size_t)grow * args.ldr + col);
                 }
             }
+            uint2 gw = make_uint2(0, 0);
+            if (fused_norm && ncols == 4) gw = *reinterpret_cast<const uint2 *>(args.norm_gain + col);
 #pragma unroll
             for (int it = 0; it < 8; ++it) {
                 const int r = 4 * it + rq, grow = row0 + r;
                 const uint4 u = ptx::ld_shared_v4(swz(b, r, sub));
                 float4 f = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
                                        __uint_as_float(u.w));
-                if (grow >= args.M || ncols <= 0) continue;
-                float *dst = args.out_f32 + (size_t)grow * args.ldo + col;
-                if (ncols == 4) {
-                    if (EPI == EPI_RESID) {
-                        f.x += res[it].x;
-                        f.y += res[it].y;
-                        f.z += res[it].z;
-                        f.w += res[it].w;
+                const bool live = grow < args.M && ncols > 0;
+                if (live) {
+                    float *dst = args.out_f32 + (size_t)grow * args.ldo + col;
+                    if (ncols == 4) {
+                        if (EPI == EPI_RESID) {
+                            f.x += res[it].x;
+                            f.y += res[it].y;
+                            f.z += res[it].z;
+                            f.w += res[it].w;
+                        }
+                        *reinterpret_cast<float4 *>(dst) = f;
+                    } else {
+                        float fe[4] = {f.x, f.y, f.z, f.w};
+                        const float *rr = args.resid + (size_t)grow * args.ldr + col;
+                        for (int e = 0; e < ncols; ++e) {
+                            fe[e] = EPI == EPI_RESID ? fe[e] + rr[e] : fe[e];
+                            dst[e] = fe[e];
+                        }
+                        f = make_float4(fe[0], ncols > 1 ? fe[1] : 0.f, ncols > 2 ? fe[2] : 0.f, 0.f);
                     }
-                    *reinterpret_cast<float4 *>(dst) = f;
-                } else {
-                    const float fe[4] = {f.x, f.y, f.z, f.w};
-                    const float *rr = args.resid + (size_t)grow * args.ldr + col;
-                    for (int e = 0; e < ncols; ++e) dst[e] = EPI == EPI_RESID ? fe[e] + rr[e] : fe[e];
                 }
+                if (fused_norm) {
+                    if (!live) f = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (live && ncols == 4)
+                        *reinterpret_cast<uint2 *>(args.norm_u + (size_t)grow * args.ldo + col) =
+                            make_uint2(pack_bf16(f.x * bf16lo(gw.x), f.y * __uint_as_float(gw.x & 0xFFFF0000u)),
+                                       pack_bf16(f.z * bf16lo(gw.y), f.w * __uint_as_float(gw.y & 0xFFFF0000u)));
+                    else if (live)
+                        for (int e = 0; e < ncols; ++e)
+                            args.norm_u[(size_t)grow * args.ldo + col + e] =
+                                __float2bfloat16_rn((&f.x)[e] * __bfloat162float(args.norm_gain[col + e]));
+                    ssacc[it] += pair_group_ss(f);
+                }
+            }
+        }
+        if (fused_norm && sub == 0) {
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int grow = row0 + 4 * it + rq;
+                if (grow < args.M) args.norm_ss[(size_t)(n0 / 256) * args.norm_ss_stride + grow] = ssacc[it];
             }
         }
     } else if (EPI == EPI_BF16) {
@@ -588,6 +645,7 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
             }
         }
     } else if (EPI == EPI_SWIGLU) {
+        const float rs = row_norm_scale(args, row0 + lane);  // this thread's row (its TMEM lane)
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {  // 128 accumulator columns (64 gate, 64 up) -> 64 outputs a pass
             const uint32_t b = buf + (c & 1) * kStageBuf;
@@ -600,8 +658,9 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
                 uint32_t p[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const float g0 = __uint_as_float(g[2 * e]), g1 = __uint_as_float(g[2 * e + 1]);
-                    p[e] = pack_bf16(silu_f(g0) * __uint_as_float(u[2 * e]), silu_f(g1) * __uint_as_float(u[2 * e + 1]));
+                    const float g0 = __uint_as_float(g[2 * e]) * rs, g1 = __uint_as_float(g[2 * e + 1]) * rs;
+                    p[e] = pack_bf16(silu_f(g0) * (__uint_as_float(u[2 * e]) * rs),
+                                     silu_f(g1) * (__uint_as_float(u[2 * e + 1]) * rs));
                 }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) ptx::st_shared_v4(swz(b, lane, 4 * h + j), p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
@@ -625,12 +684,14 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
 struct QkvRow {
     float cs[64], sn[64];
     int pos, slot;
+    float r;  // the row's RMSNorm scale (1 without the fused norm)
     bool ok;
 };
 
 __device__ __forceinline__ void qkv_preload(const GemmArgs &args, int row, bool rotates, QkvRow &R) {
     const QkvEpilogue &E = args.qkv;
     R.ok = row < args.M;
+    R.r = row_norm_scale(args, row);
     R.pos = R.ok ? E.tok_pos[row] : 0;
     R.slot = R.ok ? E.tok_slot[row] : 0;
     if (rotates && R.ok) {
@@ -668,7 +729,10 @@ __device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32
                 ptx::tmem_ld32(t_head + c * 32, u);
                 ptx::tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(u[j]), __uint_as_float(u[j]), ss);
+                for (int j = 0; j < 32; ++j) {
+                    const float v = __uint_as_float(u[j]) * R.r;
+                    ss = fmaf(v, v, ss);
+                }
             }
             r = rsqrtf(ss / 128.0f + E.eps);
         }
@@ -695,8 +759,8 @@ __device__ __forceinline__ void epilogue_qkv_staged(const GemmArgs &args, uint32
             float a[16], bb[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                a[j] = __uint_as_float(lo[j]);
-                bb[j] = __uint_as_float(hi[j]);
+                a[j] = __uint_as_float(lo[j]) * R.r;
+                bb[j] = __uint_as_float(hi[j]) * R.r;
             }
             if (rotate && R.ok) {
 #pragma unroll
@@ -1005,6 +1069,70 @@ cudaError_t launch_epi(const CUtensorMap &ta, const CUtensorMap &tb, const GemmA
 
 }  // namespace
 
+namespace {
+
+// One warp per 32 rows and 256-column group: the rows' u = bf16(gain * x) and their group sums of squares, with the
+// lanes laid over the columns as the staged residual epilogue lays them (lane = 8 rq + sub: rows 4 it + rq, columns
+// 32 c + 4 sub of pass c), so the sums come out in the same order and bits.
+__global__ void __launch_bounds__(256) pair_prep_kernel(const float *x, int T, int hidden, const __nv_bfloat16 *gain,
+                                                        __nv_bfloat16 *u, float *ss, size_t ss_stride) {
+    ptx::griddep_wait();
+    ptx::griddep_launch();
+    const int lane = threadIdx.x & 31, sub = lane & 7, rq = lane >> 3;
+    const int groups = (hidden + 255) / 256;
+    const int wg = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int row0 = (wg / groups) * 32, g = wg % groups;
+    if (row0 >= T) return;  // whole warp
+    float ssacc[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) ssacc[it] = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+        const int col = g * 256 + c * 32 + sub * 4;
+        const int ncols = min(4, hidden - col);
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+            const int row = row0 + 4 * it + rq;
+            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (row < T && ncols > 0) {
+                const float *xr = x + (size_t)row * hidden + col;
+                if (ncols == 4) {
+                    f = *reinterpret_cast<const float4 *>(xr);
+                    const uint2 gw = *reinterpret_cast<const uint2 *>(gain + col);
+                    *reinterpret_cast<uint2 *>(u + (size_t)row * hidden + col) =
+                        make_uint2(pack_bf16(f.x * bf16lo(gw.x), f.y * __uint_as_float(gw.x & 0xFFFF0000u)),
+                                   pack_bf16(f.z * bf16lo(gw.y), f.w * __uint_as_float(gw.y & 0xFFFF0000u)));
+                } else {
+                    float fe[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int e = 0; e < ncols; ++e) {
+                        fe[e] = xr[e];
+                        u[(size_t)row * hidden + col + e] = __float2bfloat16_rn(fe[e] * __bfloat162float(gain[col + e]));
+                    }
+                    f = make_float4(fe[0], fe[1], fe[2], 0.f);
+                }
+            }
+            ssacc[it] += pair_group_ss(f);
+        }
+    }
+    if (sub == 0) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+            const int row = row0 + 4 * it + rq;
+            if (row < T) ss[(size_t)g * ss_stride + row] = ssacc[it];
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_pair_prep(const float *x, int T, int hidden, const __nv_bfloat16 *gain, __nv_bfloat16 *u, float *ss,
+                             size_t ss_stride, cudaStream_t st) {
+    if (T < 1 || hidden < 4 || hidden % 4 || !x || !gain || !u || !ss) return cudaErrorInvalidValue;
+    const int warps = (T + 31) / 32 * ((hidden + 255) / 256);
+    return launch_kernel(pair_prep_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, x, T, hidden, gain, u, ss,
+                         ss_stride);
+}
+
 bool gemm_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
     return make_tmap_2d(map, ptr, rows, cols, box_rows);
 }
@@ -1035,6 +1163,12 @@ const char *gemm_check(const GemmArgs &a) {
         if (((uintptr_t)q.q_out | (uintptr_t)q.k_out | (uintptr_t)q.v_out | (uintptr_t)q.pool) & 15)
             return "the q/k/v epilogue outputs must be 16-byte aligned";
     }
+    if (a.norm_u && (a.epi != EPI_RESID || a.cta_pair != 2 || !a.norm_gain || !a.norm_ss ||
+                     a.norm_ss_stride < (size_t)a.M || ((uintptr_t)a.norm_u & 7) || ((uintptr_t)a.norm_gain & 7)))
+        return "the fused norm's outputs need EPI_RESID on CTA pairs, a gain, sums and 8-byte aligned u";
+    if (a.row_ss && ((a.epi != EPI_SWIGLU && a.epi != EPI_QKV) || a.cta_pair != 2 || a.row_nss < 1 ||
+                     a.row_hidden < 1 || a.row_ss_stride < (size_t)a.M))
+        return "a row norm scale needs EPI_SWIGLU or EPI_QKV on CTA pairs and valid sums";
     if (a.cta_pair < 0 || a.cta_pair > 2) return "cta_pair must be 0, 1 or 2";
     if (a.cta_pair == 2 && (a.bn != 256 || a.splits != 1 || a.epi == EPI_PARTIAL))
         return "CTA pairs need bn 256, one split and a non-partial epilogue";

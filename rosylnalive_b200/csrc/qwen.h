@@ -21,16 +21,10 @@ struct KvLayout {
 
 __host__ __device__ inline size_t kv_page_elems(int kv_heads) { return (size_t)kv_heads * 2 * kPageTokens * kHeadDim; }
 
-// x[t] = widen(embed[ids[t]]) (fp32 residual); xn[t] = bf16(rmsnorm(x[t]) * w).
-cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
-                              const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st);
-
-// xn[t] = bf16(rmsnorm(x[t]) * w) for the T rows of x (fp32 [T][hidden]): one warp a row (the prefill form).
-cudaError_t launch_norm_rows(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn,
-                             cudaStream_t st);
-// The same in the block-per-row form (the decode step's final norm).
+// xn[t] = bf16(rmsnorm(x[idx[t]]) * w) for t < T (rows 0..T-1 without idx), one block a row: the final norm before
+// the lm_head.
 cudaError_t launch_norm_rows_block(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
-                                   __nv_bfloat16 *xn, cudaStream_t st);
+                                   __nv_bfloat16 *xn, cudaStream_t st, const int32_t *idx = nullptr);
 
 // Paged split-K decode attention: one query per sequence (row b, slot slots[b], seq_len[slot] keys including the new
 // one), GQA group 2, pages_per_split pages per CTA; then the combine writes out bf16 [B][q_heads][128].
@@ -71,10 +65,6 @@ cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_toke
 
 // rows[r] = argmax of logits[r] ([R][V] fp32): lowest index of the maximum, 0xFFFFFFFF for a row holding a NaN.
 cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st);
-
-// dst[r] = src[idx[r]] for rows of `cols` bf16 (gathers the last row of each sequence for lm_head).
-cudaError_t launch_gather_rows(const __nv_bfloat16 *src, const int32_t *idx, int R, int cols, __nv_bfloat16 *dst,
-                               cudaStream_t st);
 
 // seq_len[slots[b]] += 1 for b < B (after a decode step's append).
 cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos, cudaStream_t st);

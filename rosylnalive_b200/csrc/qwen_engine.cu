@@ -5,16 +5,20 @@
 // final norm; tied lm_head; argmax) from the fused kernels:
 //
 //   prefill (T tokens of packed sequences)            decode step (B rows, one token each)
-//   embed_norm                                        advance (positions, lengths) ; decode_prep (embed; norm inputs)
+//   decode_prep (embed; layer 0's norm inputs)        advance (positions, lengths) ; decode_prep (embed; norm inputs)
 //   per layer:                                        per layer:
-//     GEMM xn.Wqkv^T -> qkv fp32                        GEMM Wqkv.u^T + norm scale, QK-norm, RoPE, KV append
-//     (q/k/v epilogue: q; k, v into the paged cache)    paged split-K decode attention + combine
+//     GEMM u.Wqkv^T + norm scale; q/k/v epilogue:       GEMM Wqkv.u^T + norm scale, QK-norm, RoPE, KV append
+//       QK-norm, RoPE, q; k, v into the paged cache     paged split-K decode attention + combine
 //     flash prefill attention over the cache -> attn    GEMM Wo.attn^T + x += . ; next norm's inputs
-//     GEMM attn.Wo^T, epilogue x += .                   GEMM Wgu.u^T + norm scale, SwiGLU
-//     resid_norm (post norm) -> xn                      GEMM Wdown.act^T + x += . ; next norm's inputs
-//     GEMM xn.Wgu^T, SwiGLU epilogue -> act
-//     GEMM act.Wdown^T, epilogue x += . ; resid_norm
-//   gather last rows ; lm_head GEMM ; argmax          final norm ; lm_head GEMM ; argmax
+//     GEMM attn.Wo^T: x += . ; next norm's inputs       GEMM Wgu.u^T + norm scale, SwiGLU
+//     GEMM u.Wgu^T + norm scale, SwiGLU -> act          GEMM Wdown.act^T + x += . ; next norm's inputs
+//     GEMM act.Wdown^T: x += . ; next norm's inputs
+//   final norm of the last rows ; lm_head ; argmax    final norm ; lm_head GEMM ; argmax
+//
+// RMSNorm runs inside the GEMMs on both paths: the GEMM that updates the residual stream x also writes the next
+// norm's inputs, u = bf16(gain * x) and per-column-group sums of squares of x, and the GEMM that consumes u multiplies
+// its output rows by the norm's scale 1 / sqrt(mean(x^2) + eps) (it is linear in each row), so no kernel boundary
+// waits for a whole row's norm. Prefill GEMMs run on CTA pairs (gemm_tcgen05.cu).
 //
 // Decode GEMMs swap A and B (weights fill the 128-row tensor-core tile, the B <= 64 tokens are N) and split K over a
 // cluster of CTAs that reduces through distributed shared memory and runs the consumer itself (gemm_decode.cu). A
@@ -135,11 +139,13 @@ static lrm_status qcuda(lrm_qwen q, cudaError_t e, const char *what) {
         if (e_ != cudaSuccess) return qcuda(q, e_, what); \
     } while (0)
 
+// `fused` (prefill) carries the CTA-pair choice and the fused norm's fields (norm_* outputs, row_* scale inputs).
 static lrm_status gemm(lrm_qwen Q, const void *A, const void *B, int M, int N, int K, int epi, int bn, int splits,
                        void *out, int ldo, const float *resid, int ldr, size_t split_stride,
-                       const QkvEpilogue *qkv = nullptr) {
+                       const QkvEpilogue *qkv = nullptr, const GemmArgs *fused = nullptr) {
     GemmArgs a;
     memset(&a, 0, sizeof a);
+    if (fused) a = *fused;
     if (qkv) a.qkv = *qkv;
     a.M = M;
     a.N = N;
@@ -420,7 +426,7 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     abytes += (size_t)T * H * 4 + (size_t)T * Q->qkv_rows * 4 + part * 4;
     abytes += (size_t)c.max_batch * kvh * Q->max_splits_attn * 2 * (128 + 2) * 4;
     abytes += (size_t)T * (H + qh * kHeadDim * 2 + I) * 2 + (size_t)R * H * 2;
-    abytes += (size_t)(H / 128) * R * 4;
+    abytes += (size_t)(H / 128) * (T > R ? T : R) * 4;
     abytes += 64 * 256;
     QTRY(Q.get(), cudaMalloc(&Q->amem, abytes), "activations");
     p = Q->amem;
@@ -443,8 +449,8 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     Q->attn = carve<__nv_bfloat16>(p, (size_t)T * qh * kHeadDim);
     Q->act = carve<__nv_bfloat16>(p, (size_t)T * I);
     Q->xl = carve<__nv_bfloat16>(p, (size_t)R * H);
-    Q->ss_stride = (size_t)R;
-    Q->ss = carve<float>(p, (size_t)(H / 128) * R);
+    Q->ss_stride = (size_t)(T > R ? T : R);
+    Q->ss = carve<float>(p, (size_t)(H / 128) * Q->ss_stride);
     if ((size_t)(p - Q->amem) > abytes) return qfail(Q.get(), LRM_ERR_STATE, "activation plan overflow");
     QTRY(Q.get(), cudaMallocHost(&Q->h_pinned, sizeof(uint32_t) * (size_t)T * 4), "pinned staging");
     *out = Q.release();
@@ -720,14 +726,32 @@ static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, co
     for (int i = 0; i < nseq; ++i)
         QTRY(Q, cudaMemcpyAsync(Q->d_seq_len + slots[i], &new_len[i], 4, cudaMemcpyHostToDevice, st), "seq_len");
     const int H = c.hidden, qh = c.q_heads, kvh = c.kv_heads, I = c.intermediate;
+    const int nss_pair = (H + 255) / 256;  // the residual GEMMs' norm groups (256 columns each)
     PdlScope pdl;
-    if (Q->is_first)
-        KTRY(Q, launch_embed_norm(Q->ids, T, Q->embed, H, c.vocab, Q->layers[0].in_norm, c.eps, Q->x, Q->xn, st),
-             "embed_norm");
-    else  // x[0, T) holds the previous stage's residual
-        KTRY(Q, launch_norm_rows(Q->x, T, H, Q->layers[0].in_norm, c.eps, Q->xn, st), "norm");
+    // RMSNorm fused into the GEMMs: a layer's input is u = bf16(gain * x) (in xn) with the sums of squares of x (ss);
+    // the consuming GEMM applies the norm's scale to its output rows. The first layer's inputs come from the embedding
+    // on the first stage, from the previous stage's residual (in the residual GEMMs' order) on the others.
+    int nss_in;
+    if (Q->is_first) {
+        KTRY(Q, launch_decode_prep(Q->ids, Q->embed, c.vocab, Q->x, T, H, Q->layers[0].in_norm, Q->xn, Q->ss,
+                                   Q->ss_stride, st),
+             "norm inputs");
+        nss_in = H / 128;
+    } else {
+        KTRY(Q, launch_pair_prep(Q->x, T, H, Q->layers[0].in_norm, Q->xn, Q->ss, Q->ss_stride, st), "norm inputs");
+        nss_in = nss_pair;
+    }
+    GemmArgs pair;  // every prefill GEMM runs on CTA pairs (the fused norm lives in their epilogues)
+    memset(&pair, 0, sizeof pair);
+    pair.cta_pair = 2;
     for (int l = 0; l < Q->nl; ++l) {
         const Layer &L = Q->layers[l];
+        GemmArgs scaled = pair;  // a consumer of norm inputs: its rows get the norm's scale
+        scaled.row_ss = Q->ss;
+        scaled.row_nss = nss_in;
+        scaled.row_ss_stride = Q->ss_stride;
+        scaled.row_hidden = H;
+        scaled.row_eps = c.eps;
         // q/k/v GEMM with QK-RMSNorm, RoPE and the paged KV append in its epilogue (no fp32 q/k/v round trip).
         QkvEpilogue qe;
         qe.q_out = Q->q;
@@ -745,7 +769,8 @@ static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, co
         qe.sin_t = Q->sin_t;
         qe.tok_slot = Q->tok_slot;
         qe.tok_pos = Q->tok_pos;
-        LTRY(gemm(Q, Q->xn, L.w_qkv, T, Q->qkv_rows, H, EPI_QKV, 256, 1, nullptr, Q->qkv_rows, nullptr, 0, 0, &qe));
+        LTRY(gemm(Q, Q->xn, L.w_qkv, T, Q->qkv_rows, H, EPI_QKV, 256, 1, nullptr, Q->qkv_rows, nullptr, 0, 0, &qe,
+                  &scaled));
         PrefillAttnArgs pa;
         pa.q = Q->q;
         pa.out = Q->attn;
@@ -762,15 +787,29 @@ static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, co
         pa.pages_per_seq = Q->maxp;
         pa.kv_pages = c.kv_pages;
         KTRY(Q, launch_prefill_attention_tc(pa, T, Q->err, st), "prefill_attention");
-        LTRY(gemm(Q, Q->attn, L.w_o, T, H, qh * kHeadDim, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
-        KTRY(Q, launch_norm_rows(Q->x, T, H, L.post_norm, c.eps, Q->xn, st), "norm");
-        LTRY(gemm(Q, Q->xn, L.w_gu, T, 2 * I, H, EPI_SWIGLU, 256, 1, Q->act, I, nullptr, 0, 0));
-        LTRY(gemm(Q, Q->act, L.w_down, T, H, I, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0));
-        if (const __nv_bfloat16 *next_norm = next_norm_of(Q, l))
-            KTRY(Q, launch_norm_rows(Q->x, T, H, next_norm, c.eps, Q->xn, st), "norm");
+        // o_proj: x += attn Wo^T, with the post-attention norm's inputs
+        GemmArgs post = pair;
+        post.norm_gain = L.post_norm;
+        post.norm_u = Q->xn;
+        post.norm_ss = Q->ss;
+        post.norm_ss_stride = Q->ss_stride;
+        LTRY(gemm(Q, Q->attn, L.w_o, T, H, qh * kHeadDim, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0, nullptr, &post));
+        scaled.row_nss = nss_pair;
+        LTRY(gemm(Q, Q->xn, L.w_gu, T, 2 * I, H, EPI_SWIGLU, 256, 1, Q->act, I, nullptr, 0, 0, nullptr, &scaled));
+        // down: x += act Wdown^T, with the next layer's norm inputs (none after a stage's last layer)
+        GemmArgs next = pair;
+        if (l + 1 < Q->nl) {
+            next.norm_gain = Q->layers[l + 1].in_norm;
+            next.norm_u = Q->xn;
+            next.norm_ss = Q->ss;
+            next.norm_ss_stride = Q->ss_stride;
+        }
+        LTRY(gemm(Q, Q->act, L.w_down, T, H, I, EPI_RESID, 256, 1, Q->x, H, Q->x, H, 0, nullptr, &next));
+        nss_in = nss_pair;
     }
     if (!Q->is_last) return sync_check(Q);
-    KTRY(Q, launch_gather_rows(Q->xn, Q->last_idx, nseq, H, Q->xl, st), "gather");
+    // the final norm of each sequence's last row only (the greedy head reads no other)
+    KTRY(Q, launch_norm_rows_block(Q->x, nseq, H, Q->final_norm, c.eps, Q->xl, st, Q->last_idx), "final norm");
     LTRY(gemm(Q, Q->embed, Q->xl, c.vocab, nseq, H, EPI_PARTIAL, 64, 1, Q->partial, c.vocab, nullptr, 0,
               (size_t)nseq * c.vocab));
     KTRY(Q, launch_argmax(Q->partial, nseq, c.vocab, Q->next, st), "argmax");

@@ -3,11 +3,11 @@
 // The reference computes these as separate catalog dispatches (embed_gather_bf16, rmsnorm_rows, rope_apply,
 // copy_rows, silu_mul, add, argmax_rows: src/Lrm.Shaders/hlsl/kernels/basic/*.hlsl). Here each neighbourhood is one
 // kernel so an activation makes one trip through HBM:
-//   embed_norm        embed gather + layer 0's input RMSNorm (prefill)
-//   norm_rows_*       RMSNorm rows (prefill: a warp a row; the decode step's final norm: a block a row)
-//   argmax, gather_rows, advance
-// and decode attention streams the paged bf16 KV cache with bulk async copies (see decode_attn_kernel). The decode
-// step's split-K reductions, residual adds, QK-norm/RoPE/KV append and SwiGLU run inside its GEMMs (gemm_decode.cu).
+//   norm_rows_block   RMSNorm of chosen rows before the lm_head (a block a row)
+//   argmax, advance
+// and decode attention streams the paged bf16 KV cache with bulk async copies (see decode_attn_kernel). The embedding
+// gather, the layers' RMSNorms, residual adds, QK-norm/RoPE/KV append and SwiGLU run inside the GEMMs and their prep
+// kernels (gemm_tcgen05.cu for prefill, gemm_decode.cu for decode).
 #include <cuda_bf16.h>
 #include <math.h>
 #include <stdint.h>
@@ -46,40 +46,17 @@ __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
     return make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
 }
 
-// ---- embed + norm -------------------------------------------------------------------------------------------------
-
-__global__ void __launch_bounds__(256) embed_norm_kernel(const uint32_t *ids, const __nv_bfloat16 *embed, int hidden,
-                                                         int vocab, const __nv_bfloat16 *w, float eps, float *x,
-                                                         __nv_bfloat16 *xn) {
-    ptx::griddep_wait();
-    ptx::griddep_launch();
-    __shared__ float red[8];
-    const int t = blockIdx.x;
-    uint32_t id = ids[t];
-    const bool ok = id < (uint32_t)vocab;
-    const __nv_bfloat16 *row = embed + (size_t)(ok ? id : 0) * hidden;
-    float ss = 0.f;
-    for (int c = threadIdx.x; c < hidden; c += 256) {
-        float v = ok ? bf(row[c]) : __uint_as_float(0x7FC00000u);
-        x[(size_t)t * hidden + c] = v;
-        ss += v * v;
-    }
-    float r = rsqrtf(block_sum256(ss, red) / hidden + eps);
-    for (int c = threadIdx.x; c < hidden; c += 256)
-        xn[(size_t)t * hidden + c] = __float2bfloat16_rn(x[(size_t)t * hidden + c] * r * bf(w[c]));
-}
-
 // ---- RMSNorm rows ----------------------------------------------------------------------------------------------
 
-// One block per row, 4 consecutive columns per thread (hidden % 4 == 0): xn = bf16(rmsnorm(x) * w). The decode step's
-// final norm (before the lm_head) and a pipeline stage resuming a decode step use this form.
-__global__ void __launch_bounds__(256) norm_rows_block_kernel(const float *x, int hidden, const __nv_bfloat16 *w,
-                                                              float eps, __nv_bfloat16 *xn) {
+// One block per row, 4 consecutive columns per thread (hidden % 4 == 0): xn[t] = bf16(rmsnorm(x[row]) * w) with row
+// idx[t] (t without idx): the final norm before the lm_head, of the decode step's rows or a prefill's last rows.
+__global__ void __launch_bounds__(256) norm_rows_block_kernel(const float *x, const int32_t *idx, int hidden,
+                                                              const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn) {
     ptx::griddep_wait();
     ptx::griddep_launch();
     __shared__ float red[8];
     const int t = blockIdx.x;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)t * hidden);
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)(idx ? idx[t] : t) * hidden);
     const int n4 = hidden / 4;
     float ss = 0.f;
     for (int c = threadIdx.x; c < n4; c += 256) {
@@ -93,60 +70,6 @@ __global__ void __launch_bounds__(256) norm_rows_block_kernel(const float *x, in
         *reinterpret_cast<uint2 *>(xn + (size_t)t * hidden + 4 * c) =
             pack4(v.x * r * __uint_as_float(wv.x << 16), v.y * r * __uint_as_float(wv.x & 0xFFFF0000u),
                   v.z * r * __uint_as_float(wv.y << 16), v.w * r * __uint_as_float(wv.y & 0xFFFF0000u));
-    }
-}
-
-// Prefill form (no split partials): one warp per row, 8 rows per block, the row's float4s spread over the lanes and a
-// shuffle reduction, so the many short rows of a prefill do not pay a block-wide barrier each.
-__global__ void __launch_bounds__(256) norm_rows_warp_kernel(const float *x, int T, int hidden,
-                                                             const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn) {
-    ptx::griddep_wait();
-    ptx::griddep_launch();
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= T) return;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * hidden);
-    const int n4 = hidden / 4;
-    float ss = 0.f;
-    for (int c = lane; c < n4; c += 32) {
-        const float4 v = xr[c];
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    }
-    const float r = rsqrtf(warp_sum(ss) / hidden + eps);
-    for (int c = lane; c < n4; c += 32) {
-        const float4 v = xr[c];
-        const uint2 wv = *reinterpret_cast<const uint2 *>(w + 4 * c);
-        *reinterpret_cast<uint2 *>(xn + (size_t)row * hidden + 4 * c) =
-            pack4(v.x * r * __uint_as_float(wv.x << 16), v.y * r * __uint_as_float(wv.x & 0xFFFF0000u),
-                  v.z * r * __uint_as_float(wv.y << 16), v.w * r * __uint_as_float(wv.y & 0xFFFF0000u));
-    }
-}
-
-// The same with a compile-time row width (N4 float4s, hidden 4 N4): every lane issues its N4 / 32 row loads at once
-// and keeps them in registers for the second pass. The sums run in the same order, so the results are the same bits.
-template <int N4>
-__global__ void __launch_bounds__(256) norm_rows_warp_fixed_kernel(const float *x, int T, const __nv_bfloat16 *w,
-                                                                   float eps, __nv_bfloat16 *xn) {
-    static_assert(N4 % 32 == 0, "a whole number of float4s a lane");
-    constexpr int PER = N4 / 32;
-    ptx::griddep_wait();
-    ptx::griddep_launch();
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= T) return;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * N4 * 4);
-    float4 v[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) v[i] = xr[lane + 32 * i];
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-    const float r = rsqrtf(warp_sum(ss) / (N4 * 4) + eps);
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        const int c = lane + 32 * i;
-        const uint2 wv = *reinterpret_cast<const uint2 *>(w + 4 * c);
-        *reinterpret_cast<uint2 *>(xn + (size_t)row * N4 * 4 + 4 * c) =
-            pack4(v[i].x * r * __uint_as_float(wv.x << 16), v[i].y * r * __uint_as_float(wv.x & 0xFFFF0000u),
-                  v[i].z * r * __uint_as_float(wv.y << 16), v[i].w * r * __uint_as_float(wv.y & 0xFFFF0000u));
     }
 }
 
@@ -203,14 +126,6 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V
         }
         if (threadIdx.x == 0) out[blockIdx.x] = nan_any ? 0xFFFFFFFFu : (uint32_t)idx;
     }
-}
-
-__global__ void gather_rows_kernel(const __nv_bfloat16 *src, const int32_t *idx, int cols, __nv_bfloat16 *dst) {
-    ptx::griddep_wait();
-    ptx::griddep_launch();
-    const int r = blockIdx.x;
-    const __nv_bfloat16 *s = src + (size_t)idx[r] * cols;
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[(size_t)r * cols + c] = s[c];
 }
 
 __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos) {
@@ -483,30 +398,13 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
 
 }  // namespace
 
-cudaError_t launch_embed_norm(const uint32_t *ids, int T, const __nv_bfloat16 *embed, int hidden, int vocab,
-                              const __nv_bfloat16 *w, float eps, float *x, __nv_bfloat16 *xn, cudaStream_t st) {
-    return launch_kernel(embed_norm_kernel, dim3(T), dim3(256), 0, st, ids, embed, hidden, vocab, w, eps, x, xn);
-}
-
-cudaError_t launch_norm_rows(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps, __nv_bfloat16 *xn,
-                             cudaStream_t st) {
-    if (hidden == 1024)  // Qwen3-0.6B
-        return launch_kernel(norm_rows_warp_fixed_kernel<256>, dim3((T + 7) / 8), dim3(256), 0, st, x, T, w, eps, xn);
-    return launch_kernel(norm_rows_warp_kernel, dim3((T + 7) / 8), dim3(256), 0, st, x, T, hidden, w, eps, xn);
-}
-
 cudaError_t launch_norm_rows_block(const float *x, int T, int hidden, const __nv_bfloat16 *w, float eps,
-                                   __nv_bfloat16 *xn, cudaStream_t st) {
-    return launch_kernel(norm_rows_block_kernel, dim3(T), dim3(256), 0, st, x, hidden, w, eps, xn);
+                                   __nv_bfloat16 *xn, cudaStream_t st, const int32_t *idx) {
+    return launch_kernel(norm_rows_block_kernel, dim3(T), dim3(256), 0, st, x, idx, hidden, w, eps, xn);
 }
 
 cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st) {
     return launch_kernel(argmax_kernel, dim3(R), dim3(1024), 0, st, logits, V, out);
-}
-
-cudaError_t launch_gather_rows(const __nv_bfloat16 *src, const int32_t *idx, int R, int cols, __nv_bfloat16 *dst,
-                               cudaStream_t st) {
-    return launch_kernel(gather_rows_kernel, dim3(R), dim3(256), 0, st, src, idx, cols, dst);
 }
 
 cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos, cudaStream_t st) {
