@@ -204,6 +204,34 @@ typedef struct lrm_gemm_desc {
 } lrm_gemm_desc;
 lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *desc);
 
+/* A decode step's weight GEMM with its consumer fused, the form the engine's decode step runs: Y = W * B^T for
+ * weights w bf16 [m, k] (m a multiple of 128) and n tokens b bf16 [n, k], K split over a thread-block cluster of
+ * `splits` CTAs (1, 2, 3, 4, 8 or 16; 0 chooses) whose accumulators are added through distributed shared memory in
+ * split order. Replaces the reference's matmul_bf16w (src/Lrm.Shaders/hlsl/kernels/matmul/matmul_bf16w.hlsl) plus the
+ * add / rmsnorm_rows / silu_mul dispatches that follow it in a decode step.
+ *   LRM_DEC_RESID   x [n][m] fp32 += Y; with gain (bf16 [m]) also u [n][m] = bf16(gain * x) and
+ *                   ss_out[m / 128][t] (row stride ss_stride) = the sum of x^2 over each 128-column group: the next
+ *                   RMSNorm's inputs;
+ *   LRM_DEC_SWIGLU  the norm scale r[t] = 1 / sqrt(sum_g ss[g][t] / hidden + eps) (g < nss) applied to Y's rows, whose
+ *                   weight rows interleave gate and up in blocks of 64; act [n][ld_act] bf16 = silu(r g) * (r u).
+ * The q/k/v form (norm scale, QK-norm, RoPE, paged KV append) runs inside the engine only. */
+#define LRM_DEC_SWIGLU 1
+#define LRM_DEC_RESID 2
+typedef struct lrm_decode_gemm_desc {
+    int32_t m, n, k;
+    uint64_t w, b;
+    int32_t epilogue; /* LRM_DEC_* */
+    int32_t splits;   /* 0 chooses */
+    uint64_t ss;      /* SWIGLU: fp32 [nss][ss_stride] */
+    int32_t nss, hidden;
+    uint64_t ss_stride;
+    float eps;
+    uint64_t x, gain, u, ss_out; /* RESID */
+    uint64_t act;                /* SWIGLU */
+    int32_t ld_act;
+} lrm_decode_gemm_desc;
+lrm_status lrm_op_decode_gemm(void *stream, const lrm_decode_gemm_desc *desc);
+
 /* Causal GQA attention of packed sequences (each starting at position 0), bf16 in/out, fp32 softmax and
  * accumulation: q [T, q_heads, 128], k/v [T, kv_heads, 128] (K after QK-norm and RoPE), cu_seqlens int32 [nseq + 1]
  * (device, cu_seqlens[nseq] = total_tokens = T), out [T, q_heads, 128]. Runs on the tcgen05 tensor cores (TMA tiles,

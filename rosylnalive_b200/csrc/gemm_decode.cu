@@ -27,6 +27,9 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <string>
+
+#include "../../include/lrm_cuda.h"
 #include "gemm.h"
 #include "internal.h"
 #include "ptx.cuh"
@@ -521,3 +524,48 @@ cudaError_t launch_decode_prep(const uint32_t *ids, const __nv_bfloat16 *embed, 
 }
 
 }  // namespace lrm
+
+namespace lrm {
+uint32_t *device_error_word();
+int device_sms();
+lrm_status op_fail(lrm_status s, const std::string &m);
+lrm_status op_cuda(cudaError_t e, const char *what);
+}  // namespace lrm
+
+extern "C" lrm_status lrm_op_decode_gemm(void *stream, const lrm_decode_gemm_desc *d) {
+    using namespace lrm;
+    if (!d) return op_fail(LRM_ERR_ARGUMENT, "decode gemm: descriptor is null");
+    if (d->epilogue != LRM_DEC_RESID && d->epilogue != LRM_DEC_SWIGLU)
+        return op_fail(LRM_ERR_ARGUMENT, "decode gemm: the epilogue must be LRM_DEC_RESID or LRM_DEC_SWIGLU");
+    if (d->m < 1 || d->n < 1 || d->k < 1) return op_fail(LRM_ERR_ARGUMENT, "decode gemm: sizes must be positive");
+    DecodeGemmArgs a;
+    memset(&a, 0, sizeof a);
+    a.M = d->m;
+    a.N = d->n;
+    a.K = d->k;
+    a.A = (const void *)d->w;
+    a.B = (const void *)d->b;
+    a.epi = d->epilogue == LRM_DEC_RESID ? DEC_RESID : DEC_SWIGLU;
+    a.splits = d->splits ? d->splits : decode_gemm_splits(d->m, d->k, device_sms());
+    const int nkb = (d->k + kBK - 1) / kBK;
+    a.kb_per_split = a.splits > 0 ? (nkb + a.splits - 1) / a.splits : 0;
+    a.ss_stride = (size_t)d->ss_stride;
+    if (a.epi == DEC_SWIGLU) {
+        a.ss = (const float *)d->ss;
+        a.nss = d->nss;
+        a.hidden = d->hidden;
+        a.eps = d->eps;
+        a.act = (__nv_bfloat16 *)d->act;
+        a.ld_act = d->ld_act;
+    } else {
+        a.x = (float *)d->x;
+        a.gain = (const __nv_bfloat16 *)d->gain;
+        a.u = (__nv_bfloat16 *)d->u;
+        a.ss_out = (float *)d->ss_out;
+    }
+    a.err = device_error_word();
+    if (!a.err) return LRM_ERR_CUDA;
+    if (const char *why = decode_gemm_check(a)) return op_fail(LRM_ERR_ARGUMENT, std::string("decode gemm: ") + why);
+    return op_cuda(decode_gemm_launch(a, (cudaStream_t)stream), "decode gemm");
+}
+

@@ -500,19 +500,21 @@ __device__ __forceinline__ void store_bf16_tail(__nv_bfloat16 *dst, uint4 v, int
     }
 }
 
-// One pass's share of a row's sum of squares in the staged epilogue: the lane's four columns (fused multiply-adds in
-// order), then a butterfly over the eight lanes that hold the row's 32 columns of the pass (lanes 8 rq .. 8 rq + 7),
-// which leaves the same bits in all eight. A row's 256-column total adds the eight passes in order. pair_prep_kernel
-// computes the same sums from the residual stream in the same order.
-__device__ __forceinline__ float pair_group_ss(float4 f) {
-    float p = f.x * f.x;
-    p = fmaf(f.y, f.y, p);
-    p = fmaf(f.z, f.z, p);
-    p = fmaf(f.w, f.w, p);
-    p += __shfl_xor_sync(0xffffffffu, p, 1);
-    p += __shfl_xor_sync(0xffffffffu, p, 2);
-    p += __shfl_xor_sync(0xffffffffu, p, 4);
-    return p;
+// A row's sum of squares over a 256-column tile in the staged epilogue, in two steps. Each lane adds the squares of
+// its four columns of every pass to its own partial (fused multiply-adds in pass, then column order: lane_ss), and
+// after the eight passes a butterfly over the eight lanes that hold the row (lanes 8 rq .. 8 rq + 7: row_ss) leaves
+// the total, the same bits in all eight. pair_prep_kernel computes the same sums from the residual stream in the
+// same order.
+__device__ __forceinline__ float lane_ss(float4 f, float acc) {
+    acc = fmaf(f.x, f.x, acc);
+    acc = fmaf(f.y, f.y, acc);
+    acc = fmaf(f.z, f.z, acc);
+    return fmaf(f.w, f.w, acc);
+}
+__device__ __forceinline__ float row_ss(float lane_partial) {
+    lane_partial += __shfl_xor_sync(0xffffffffu, lane_partial, 1);
+    lane_partial += __shfl_xor_sync(0xffffffffu, lane_partial, 2);
+    return lane_partial + __shfl_xor_sync(0xffffffffu, lane_partial, 4);
 }
 
 // The RMSNorm scale of output row m for a consumer GEMM whose A rows are bf16(gain * x): the row's group sums added
@@ -531,8 +533,8 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
                                                 uint32_t buf, int lane) {
     const int sub = lane & 7, rq = lane >> 3;  // read-back: 16-byte chunk, row within each group of four
     if (EPI == EPI_F32 || EPI == EPI_RESID) {
-        // With the fused norm (EPI_RESID and norm_u): the row's sum of squares over this 256-column tile, one entry
-        // per row the lane writes (rows 4 it + rq); see pair_group_ss.
+        // With the fused norm (EPI_RESID and norm_u): the lane's partial sums of squares of the rows it writes (rows
+        // 4 it + rq) over this 256-column tile; see lane_ss / row_ss.
         const bool fused_norm = EPI == EPI_RESID && args.norm_u != nullptr;
         float ssacc[8];
 #pragma unroll
@@ -597,15 +599,16 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &args, uint32_t t
                         for (int e = 0; e < ncols; ++e)
                             args.norm_u[(size_t)grow * args.ldo + col + e] =
                                 __float2bfloat16_rn((&f.x)[e] * __bfloat162float(args.norm_gain[col + e]));
-                    ssacc[it] += pair_group_ss(f);
+                    ssacc[it] = lane_ss(f, ssacc[it]);
                 }
             }
         }
-        if (fused_norm && sub == 0) {
+        if (fused_norm) {
 #pragma unroll
             for (int it = 0; it < 8; ++it) {
+                const float total = row_ss(ssacc[it]);
                 const int grow = row0 + 4 * it + rq;
-                if (grow < args.M) args.norm_ss[(size_t)(n0 / 256) * args.norm_ss_stride + grow] = ssacc[it];
+                if (sub == 0 && grow < args.M) args.norm_ss[(size_t)(n0 / 256) * args.norm_ss_stride + grow] = total;
             }
         }
     } else if (EPI == EPI_BF16) {
@@ -1003,14 +1006,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_tiled() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
+    // resolved once per process (a function-local static: thread-safe initialisation)
+    static const EncodeTiledFn fn = [] {
         void *p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    }
+            return (EncodeTiledFn)p;
+        return (EncodeTiledFn) nullptr;
+    }();
     return fn;
 }
 
@@ -1111,15 +1115,14 @@ __global__ void __launch_bounds__(256) pair_prep_kernel(const float *x, int T, i
                     f = make_float4(fe[0], fe[1], fe[2], 0.f);
                 }
             }
-            ssacc[it] += pair_group_ss(f);
+            ssacc[it] = lane_ss(f, ssacc[it]);
         }
     }
-    if (sub == 0) {
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
-            const int row = row0 + 4 * it + rq;
-            if (row < T) ss[(size_t)g * ss_stride + row] = ssacc[it];
-        }
+    for (int it = 0; it < 8; ++it) {
+        const float total = row_ss(ssacc[it]);
+        const int row = row0 + 4 * it + rq;
+        if (sub == 0 && row < T) ss[(size_t)g * ss_stride + row] = total;
     }
 }
 

@@ -74,21 +74,38 @@ __global__ void __launch_bounds__(256) norm_rows_block_kernel(const float *x, co
 }
 
 // ---- argmax -------------------------------------------------------------------------------------------------
+//
+// One row a cluster of kArgmaxCtas CTAs: CTA r scans the r-th contiguous part of the row (the larger value, then the
+// lower index; NaN noted), and rank 0 merges the parts over distributed shared memory. The result does not depend on
+// the split: the lowest index of the maximum, or 0xFFFFFFFF for a row that holds a NaN.
+constexpr int kArgmaxCtas = 8;
 
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V, uint32_t *out) {
+__device__ __forceinline__ void arg_merge(float &best, int &idx, float v2, int i2) {
+    if (i2 >= 0 && (idx < 0 || v2 > best || (v2 == best && i2 < idx))) {
+        best = v2;
+        idx = i2;
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float *logits, int V, uint32_t *out) {
     ptx::griddep_wait();
     ptx::griddep_launch();
-    __shared__ float sv[32];
-    __shared__ int si[32];
+    __shared__ float sv[8];
+    __shared__ int si[8];
     __shared__ int nan_any;
-    const float *row = logits + (size_t)blockIdx.x * V;
+    __shared__ __align__(16) float part[4];  // this CTA's (value, index, NaN seen) for rank 0
+    const int rank = blockIdx.x;             // the cluster rank: clusters of kArgmaxCtas along x
+    const float *row = logits + (size_t)blockIdx.y * V;
+    const int chunk = (V + kArgmaxCtas - 1) / kArgmaxCtas;
+    const int c0 = rank * chunk, c1 = min(V, c0 + chunk);
     if (threadIdx.x == 0) nan_any = 0;
     __syncthreads();
     float best = -INFINITY;
     int idx = -1;
     bool nan = false;
-    for (int c = threadIdx.x; c < V; c += 1024) {
-        float v = row[c];
+#pragma unroll 4
+    for (int c = c0 + threadIdx.x; c < c1; c += 256) {
+        const float v = row[c];
         if (isnan(v))
             nan = true;
         else if (idx < 0 || v > best) {
@@ -97,35 +114,40 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int V
         }
     }
     if (nan) nan_any = 1;
-    // warp reduce: larger value, then lower index
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float v2 = __shfl_xor_sync(FULL, best, o);
-        int i2 = __shfl_xor_sync(FULL, idx, o);
-        if (i2 >= 0 && (idx < 0 || v2 > best || (v2 == best && i2 < idx))) {
-            best = v2;
-            idx = i2;
-        }
-    }
+    for (int o = 16; o > 0; o >>= 1) arg_merge(best, idx, __shfl_xor_sync(FULL, best, o), __shfl_xor_sync(FULL, idx, o));
     if ((threadIdx.x & 31) == 0) {
         sv[threadIdx.x >> 5] = best;
         si[threadIdx.x >> 5] = idx;
     }
     __syncthreads();
     if (threadIdx.x < 32) {
-        best = sv[threadIdx.x];
-        idx = si[threadIdx.x];
+        best = threadIdx.x < 8 ? sv[threadIdx.x] : -INFINITY;
+        idx = threadIdx.x < 8 ? si[threadIdx.x] : -1;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float v2 = __shfl_xor_sync(FULL, best, o);
-            int i2 = __shfl_xor_sync(FULL, idx, o);
-            if (i2 >= 0 && (idx < 0 || v2 > best || (v2 == best && i2 < idx))) {
-                best = v2;
-                idx = i2;
-            }
+        for (int o = 4; o > 0; o >>= 1)
+            arg_merge(best, idx, __shfl_xor_sync(FULL, best, o), __shfl_xor_sync(FULL, idx, o));
+        if (threadIdx.x == 0) {
+            part[0] = best;
+            part[1] = __int_as_float(idx);
+            part[2] = __int_as_float(nan_any);
         }
-        if (threadIdx.x == 0) out[blockIdx.x] = nan_any ? 0xFFFFFFFFu : (uint32_t)idx;
     }
+    ptx::cluster_sync();  // every part is in its CTA's shared memory
+    if (rank == 0 && threadIdx.x < 32) {
+        float4 p = make_float4(-INFINITY, __int_as_float(-1), __int_as_float(0), 0.f);
+        if (threadIdx.x < kArgmaxCtas) p = ptx::ld_cluster_f4(ptx::mapa(part, threadIdx.x));
+        best = p.x;
+        idx = __float_as_int(p.y);
+        int any = __float_as_int(p.z);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+            arg_merge(best, idx, __shfl_xor_sync(FULL, best, o), __shfl_xor_sync(FULL, idx, o));
+            any |= __shfl_xor_sync(FULL, any, o);
+        }
+        if (threadIdx.x == 0) out[blockIdx.y] = any ? 0xFFFFFFFFu : (uint32_t)idx;
+    }
+    ptx::cluster_sync();  // rank 0 has read every part before any CTA leaves
 }
 
 __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos) {
@@ -404,7 +426,20 @@ cudaError_t launch_norm_rows_block(const float *x, int T, int hidden, const __nv
 }
 
 cudaError_t launch_argmax(const float *logits, int R, int V, uint32_t *out, cudaStream_t st) {
-    return launch_kernel(argmax_kernel, dim3(R), dim3(1024), 0, st, logits, V, out);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kArgmaxCtas, R);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kArgmaxCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, V, out);
 }
 
 cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_t *tok_pos, cudaStream_t st) {

@@ -32,6 +32,14 @@ class DecodeAttnDesc(ctypes.Structure):
                 ("pages_per_seq", I32), ("pages_per_split", I32), ("scale", ctypes.c_float)]
 
 
+class DecodeGemmDesc(ctypes.Structure):
+    _fields_ = [("m", I32), ("n", I32), ("k", I32), ("w", U64), ("b", U64), ("epilogue", I32), ("splits", I32),
+                ("ss", U64), ("nss", I32), ("hidden", I32), ("ss_stride", U64), ("eps", ctypes.c_float),
+                ("x", U64), ("gain", U64), ("u", U64), ("ss_out", U64), ("act", U64), ("ld_act", I32)]
+
+
+DEC_SWIGLU, DEC_RESID = 1, 2
+
 N.extra_signatures({
     "lrm_op_set_device": [I32],
     "lrm_op_error_word": [ctypes.POINTER(U32), I32],
@@ -41,6 +49,7 @@ N.extra_signatures({
     "lrm_op_decode_attention": [P, ctypes.POINTER(DecodeAttnDesc)],
     "lrm_op_decode_attention_static": [P, ctypes.POINTER(DecodeAttnDesc)],
     "lrm_op_wait_probe": [P, U32, U32],
+    "lrm_op_decode_gemm": [P, ctypes.POINTER(DecodeGemmDesc)],
 }, {"lrm_op_decode_attention_workspace": U64})
 
 # Scratch built into liblrmcuda.so for lrm_op_decode_attention_static (LRM_DECODE_ATTN_STATIC_SCRATCH_BYTES).
@@ -82,6 +91,28 @@ def gemm(a, b, out, epilogue=GEMM_F32, resid=None, splits=1, bn=0, ldo=None, spl
                  resid.data_ptr() if resid is not None else 0, resid.shape[-1] if resid is not None else 0,
                  split_stride, cta_pair)
     N.check(N.lib().lrm_op_gemm_bf16(_stream(stream), ctypes.byref(d)), None, "gemm")
+
+
+def decode_gemm_resid(w, b, x, gain=None, u=None, ss_out=None, splits=0, stream=None):
+    """x [n, m] fp32 += b @ w.T (w bf16 [m, k], b bf16 [n, k]); with gain also u [n, m] = bf16(gain * x) and
+    ss_out [m / 128, n] = the sums of x^2 over 128-column groups. K split over a cluster of `splits` CTAs."""
+    m, k = w.shape
+    n = b.shape[0]
+    d = DecodeGemmDesc(m, n, k, w.data_ptr(), b.data_ptr(), DEC_RESID, splits, 0, 0, 0,
+                       ss_out.shape[1] if ss_out is not None else 0, 0.0, x.data_ptr(),
+                       gain.data_ptr() if gain is not None else 0, u.data_ptr() if u is not None else 0,
+                       ss_out.data_ptr() if ss_out is not None else 0, 0, 0)
+    N.check(N.lib().lrm_op_decode_gemm(_stream(stream), ctypes.byref(d)), None, "decode_gemm")
+
+
+def decode_gemm_swiglu(w, b, ss, hidden, eps, act, splits=0, stream=None):
+    """act [n, m / 2] bf16 = silu(r g) * (r u) of y = b @ w.T (gate and up rows of w interleaved in blocks of 64),
+    r[t] = 1 / sqrt(sum_g ss[g, t] / hidden + eps)."""
+    m, k = w.shape
+    n = b.shape[0]
+    d = DecodeGemmDesc(m, n, k, w.data_ptr(), b.data_ptr(), DEC_SWIGLU, splits, ss.data_ptr(), ss.shape[0], hidden,
+                       ss.shape[1], eps, 0, 0, 0, 0, act.data_ptr(), act.shape[1])
+    N.check(N.lib().lrm_op_decode_gemm(_stream(stream), ctypes.byref(d)), None, "decode_gemm")
 
 
 def prefill_attention(q, k, v, out, cu_seqlens, max_len, scale, stream=None):

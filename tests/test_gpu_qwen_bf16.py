@@ -160,6 +160,29 @@ def test_decode_batch_invariance(mini):
     assert np.array_equal(alone[0], batch[0])
 
 
+def test_decode_more_than_one_token_tile(mini):
+    """A decode step of 100 sequences spans two 64-token tiles of every decode GEMM (and a 100-row prefill two CTA-pair
+    row tiles): each row's logits equal, bit for bit, those of the same sequence decoded in a batch of four, and the
+    first rows of each tile match the oracle within the bf16 bar."""
+    cfg, om, _ = mini
+    weights = S.random_weights(cfg, seed=0)
+    cos, sin = R.t_spec(R.torch_inv_freq_bits(cfg.rope_theta, cfg.head_dim), cfg.max_pos)
+    n = 100
+    prompts = [S.random_prompt(cfg.vocab, 5 + i % 23, seed=400 + i, stream=f"t{i}") for i in range(n)]
+    with Qw.QwenEngine(cfg, weights, cos, sin, max_seqs=n, max_tokens=4096, max_batch=n) as eng:
+        ids, logits = eng.greedy(prompts, 3, want_logits=True)
+        for group in ([0, 1, 63, 64], [65, 98, 99, 30]):
+            g_ids, g_logits = eng.greedy([prompts[i] for i in group], 3, slots=list(range(4)), want_logits=True)
+            for j, i in enumerate(group):
+                assert np.array_equal(g_ids[j], ids[i]), i
+                assert np.array_equal(g_logits[j].view(np.uint32), logits[i].view(np.uint32)), i
+    for i in (0, 64, 99):
+        ref_ids, ref_logits = O.greedy(om, prompts[i], 3, "f32", return_logits=True)
+        for s in range(3):
+            assert cosine(logits[i, s], ref_logits[s]) >= 0.9999, (i, s)
+            assert np.max(np.abs(logits[i, s] - ref_logits[s])) <= 2e-2, (i, s)
+
+
 def test_engine_rejects_bad_input(mini):
     cfg, om, eng = mini
     with pytest.raises(ValueError):
