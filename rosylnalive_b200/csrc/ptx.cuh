@@ -241,6 +241,16 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint3
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// (d0, d1) = (a0 * b0 + c0, a1 * b1 + c1) in one instruction on the packed fp32 pipe (fma.rn.f32x2, sm_100);
+// each lane is the same correctly rounded fma as fmaf.
+__device__ __forceinline__ void fma_x2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0,
+                                       float c1) {
+    asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
 // Brings `bytes` (a multiple of 16, 16-byte aligned) at `gmem` into L2 without waiting.
 __device__ __forceinline__ void prefetch_l2_bulk(const void *gmem, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)gmem), "r"(bytes) : "memory");

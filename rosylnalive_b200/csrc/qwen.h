@@ -40,6 +40,12 @@ struct DecodeAttnArgs {
     float *part_ml;          // [B][kv_heads][max_splits][2][2]
     __nv_bfloat16 *out;      // [B][q_heads][128]
     uint32_t *err;
+    // Set only when no kernel that can still be running once the previous kernel's CTAs have all started writes
+    // slots, seq_len, the page table or any cached K/V other than the new token's (in each row's last page): then
+    // those are read, and a split's first pages other than a row's last page are loaded, before the previous kernel
+    // completes (the engine's decode step, where the previous kernel appends the new token and writes q). Otherwise
+    // everything is read after it.
+    bool early_pages = false;
 };
 // A row whose seq_len is below 1 or needs more pages than its page-table row (or than max_splits splits hold) is
 // not read: the attention kernel writes kErrDecodeLen into err and the combine writes the row's output as zeros.

@@ -268,6 +268,7 @@ static lrm_status decode_step(lrm_qwen Q, int B, bool timed = false) {
         da.part_ml = Q->part_ml;
         da.out = Q->attn;
         da.err = Q->err;
+        da.early_pages = true;  // the q/k/v GEMM before it writes only q and the new token's K/V
         if (timed) KTRY(Q, cudaEventRecordWithFlags(Q->attn_ev[2 * l], st, cudaEventRecordExternal), "event");
         KTRY(Q, launch_decode_attention(da, st), "decode_attention");
         if (timed) KTRY(Q, cudaEventRecordWithFlags(Q->attn_ev[2 * l + 1], st, cudaEventRecordExternal), "event");

@@ -170,9 +170,12 @@ __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, in
 //           loads, conflict-free), keeps 16 partial dots (8 keys x 2 heads) and a 4-step shuffle reduce-scatter
 //           over the 16 lanes leaves lane li with the full score of key 2 (li / 2) + half for head li % 2;
 //   softmax: log2 domain (scale folded with log2 e), running maximum per head, lane-local sums;
-//   values: lane owns dims 4 lane .. 4 lane + 3 (8-byte smem loads), weights broadcast from shared memory.
-// The four warps' states merge in shared memory and the split's (max, sum, unnormalised output) go to part_*; the
-// combine kernel merges the splits.
+//   values: lane owns dims 4 lane .. 4 lane + 3 (8-byte smem loads), weights broadcast from shared memory as
+//           (p_h0, p_h0, p_h1, p_h1), so each pair of dims and head is one packed f32x2 fma.
+// The four warps' states merge in shared memory (each warp's output vectors in its own stage, which no copy targets
+// once the warp's pages are done) and the split's (max, sum, unnormalised output) go to part_*; the combine kernel
+// merges the splits. With max_splits == 1 (a batch large enough to fill the GPU with one CTA per row and kv head)
+// the CTA writes the normalised output itself and no combine runs.
 // A row's key count is usable when it is at least 1 and its pages fit both the page-table row and the max_splits
 // split states per (row, kv head) that the scratch holds; anything else would read another row's pages or states.
 __device__ __forceinline__ bool decode_len_ok(const DecodeAttnArgs &a, int len) {
@@ -182,7 +185,7 @@ __device__ __forceinline__ bool decode_len_ok(const DecodeAttnArgs &a, int len) 
 }
 
 template <int ST>
-__global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
+__global__ void __launch_bounds__(160, 6) decode_attn_kernel(DecodeAttnArgs a) {
     // Consumer warp w takes the pages j = w (mod 4) and page j sits in stage j % ST. With ST a multiple of 4 every
     // stage belongs to one warp, which waits on it phase after phase. Otherwise a warp running ahead could wait on a
     // phase two beyond the barrier's current one, which the parity test cannot tell from a completed phase.
@@ -190,29 +193,38 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
     constexpr int PAGE_BYTES = 2 * kPageTokens * kHeadDim * 2;  // K + V of one head = 8 KiB
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *stages = smem_raw;
-    float *pbuf = (float *)(stages + ST * PAGE_BYTES);  // [4][32]
-    float *red_acc = pbuf + 4 * 32;                     // [4][2][128]
-    float *red_m = red_acc + 4 * 2 * 128;               // [4][2]
+    float *pbuf = (float *)(stages + ST * PAGE_BYTES);  // [4 warps][16 keys][4]
+    float *red_m = pbuf + 4 * 64;                       // [4][2]
     float *red_l = red_m + 8;                           // [4][2]
     uint64_t *full = (uint64_t *)(red_l + 8);
     uint64_t *empty = full + ST;
 
-    ptx::griddep_wait();
-    ptx::griddep_launch();
+    // Dependents may launch only after this kernel's wait: the combine reads its row's inputs before its own wait.
+    if (!a.early_pages) {
+        ptx::griddep_wait();
+        ptx::griddep_launch();
+    }
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = a.slots[b];
+    const int32_t *ptab = a.kv.pages + (size_t)slot * a.kv.max_pages_per_seq;
+    const int p0 = split * a.pages_per_split;
+    // The producer warp fetches the split's first 32 page ids (one coalesced load, issued before the row's length
+    // is known; entries past the row's pages are never used), so no bulk copy waits on its own page-table load.
+    int pg = 0;
+    if (warp == 4 && p0 + lane < a.kv.max_pages_per_seq) pg = ptab[p0 + lane];
     const int len = a.seq_len[slot];
     if (!decode_len_ok(a, len)) {  // keys beyond the page table: nothing is read, the host sees the code
         if (split == 0 && h == 0 && threadIdx.x == 0) atomicCAS(a.err, 0u, kErrDecodeLen);
+        if (a.max_splits == 1 && threadIdx.x < 128)  // no combine follows: the row's two q heads are written as zeros
+            for (int hh = 0; hh < 2; ++hh)
+                a.out[((size_t)b * a.q_heads + 2 * h + hh) * kHeadDim + threadIdx.x] = __float2bfloat16_rn(0.f);
         return;
     }
     const int npages = (len + kPageTokens - 1) / kPageTokens;
-    const int p0 = split * a.pages_per_split;
     if (p0 >= npages) return;  // whole CTA, before any barrier
     const int n = min(npages - p0, a.pages_per_split);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t page_elems = kv_page_elems(a.kv.kv_heads);
-    const int32_t *ptab = a.kv.pages + (size_t)slot * a.kv.max_pages_per_seq;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -222,20 +234,46 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
         ptx::fence_barrier_init();
     }
     __syncthreads();
+    int pre = 0;  // pages issued before the previous kernel completed (early_pages)
+    if (a.early_pages) {
+        if (warp == 4) {
+            pre = max(0, min(min(n, ST), npages - 1 - p0));  // never the row's last page, where the new token lands
+            for (int j = 0; j < pre; ++j) {
+                const int page = __shfl_sync(FULL, pg, j);
+                if (lane == 0) {
+                    ptx::mbar_arrive_expect_tx(&full[j], PAGE_BYTES);
+                    ptx::bulk_load(stages + j * PAGE_BYTES,
+                                   a.kv.pool + (size_t)page * page_elems + (size_t)h * 2 * kPageTokens * kHeadDim,
+                                   PAGE_BYTES, &full[j]);
+                }
+            }
+        }
+        ptx::griddep_wait();
+        ptx::griddep_launch();
+    }
 
     if (warp == 4) {
-        if (lane == 0) {
-            int j = 0;
-            for (; j < n; ++j) {
-                const int s = j % ST;
-                if (!ptx::mbar_wait(&empty[s], ((j / ST) & 1) ^ 1, a.err, 0x2001)) break;
-                const __nv_bfloat16 *src = a.kv.pool + (size_t)ptab[p0 + j] * page_elems +
-                                           (size_t)h * 2 * kPageTokens * kHeadDim;
-                ptx::mbar_arrive_expect_tx(&full[s], PAGE_BYTES);
-                ptx::bulk_load(stages + s * PAGE_BYTES, src, PAGE_BYTES, &full[s]);
+        // The whole warp walks the pages (lane j % 32 holds page j's id; the next 32 ids load in one go when the
+        // walk reaches them) and lane 0 issues the copies.
+        int j = pre;
+        for (; j < n; ++j) {
+            if ((j & 31) == 0 && j > 0) pg = p0 + j + lane < a.kv.max_pages_per_seq ? ptab[p0 + j + lane] : 0;
+            const int page = __shfl_sync(FULL, pg, j & 31);
+            const int s = j % ST;
+            int ok = 1;
+            if (lane == 0) {
+                ok = ptx::mbar_wait(&empty[s], ((j / ST) & 1) ^ 1, a.err, 0x2001);
+                if (ok) {
+                    const __nv_bfloat16 *src =
+                        a.kv.pool + (size_t)page * page_elems + (size_t)h * 2 * kPageTokens * kHeadDim;
+                    ptx::mbar_arrive_expect_tx(&full[s], PAGE_BYTES);
+                    ptx::bulk_load(stages + s * PAGE_BYTES, src, PAGE_BYTES, &full[s]);
+                }
             }
-            for (int k = j > ST ? j - ST : 0; k < j; ++k) ptx::mbar_wait(&full[k % ST], (k / ST) & 1, a.err, 0x2002);
+            if (!__shfl_sync(FULL, ok, 0)) break;
         }
+        if (lane == 0)
+            for (int k = j > ST ? j - ST : 0; k < j; ++k) ptx::mbar_wait(&full[k % ST], (k / ST) & 1, a.err, 0x2002);
     } else {
         const int half = lane >> 4, li = lane & 15;
         float q0[8], q1[8];
@@ -254,7 +292,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
         }
         float m_run = -INFINITY, l_lane = 0.f;
         float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
-        float *pw = pbuf + warp * 32;
+        float *pw = pbuf + warp * 64;
         for (int j = warp; j < n; j += 4) {
             const int s = j % ST;
             if (!ptx::mbar_wait(&full[s], (j / ST) & 1, a.err, 0x2003)) break;
@@ -267,17 +305,16 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
             for (int i = 0; i < 8; ++i) {
                 const uint4 kr = *reinterpret_cast<const uint4 *>(kb + (2 * i + half) * 256 + li * 16);
                 const uint32_t w[4] = {kr.x, kr.y, kr.z, kr.w};
-                float d0 = 0.f, d1 = 0.f;
+                // even and odd dims accumulate in the two halves of a packed pair, summed at the end
+                float d0e = 0.f, d0o = 0.f, d1e = 0.f, d1o = 0.f;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float ka = __uint_as_float(w[e] << 16), kb2 = __uint_as_float(w[e] & 0xFFFF0000u);
-                    d0 = fmaf(q0[2 * e], ka, d0);
-                    d0 = fmaf(q0[2 * e + 1], kb2, d0);
-                    d1 = fmaf(q1[2 * e], ka, d1);
-                    d1 = fmaf(q1[2 * e + 1], kb2, d1);
+                    ptx::fma_x2(d0e, d0o, q0[2 * e], q0[2 * e + 1], ka, kb2, d0e, d0o);
+                    ptx::fma_x2(d1e, d1o, q1[2 * e], q1[2 * e + 1], ka, kb2, d1e, d1o);
                 }
-                v[2 * i] = d0;
-                v[2 * i + 1] = d1;
+                v[2 * i] = d0e + d0o;
+                v[2 * i + 1] = d1e + d1o;
             }
             // reduce-scatter over the 16 lanes of this half: lane li ends with value index li
 #pragma unroll
@@ -303,7 +340,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
             const float p = exp2f(sc - m_new);
             m_run = m_new;
             l_lane = l_lane * alpha + p;
-            pw[key * 2 + (li & 1)] = p;
+            *reinterpret_cast<float2 *>(pw + key * 4 + (li & 1) * 2) = make_float2(p, p);
             const float al0 = __shfl_sync(FULL, alpha, 0), al1 = __shfl_sync(FULL, alpha, 1);
             __syncwarp();
 #pragma unroll
@@ -313,17 +350,13 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
             }
             for (int t = 0; t < valid; ++t) {
                 const uint2 vr = *reinterpret_cast<const uint2 *>(vb + t * 256 + lane * 8);
-                const float2 pp = *reinterpret_cast<const float2 *>(pw + 2 * t);
+                const float4 pp = *reinterpret_cast<const float4 *>(pw + 4 * t);
                 const float va = __uint_as_float(vr.x << 16), vb2 = __uint_as_float(vr.x & 0xFFFF0000u),
                             vc = __uint_as_float(vr.y << 16), vd = __uint_as_float(vr.y & 0xFFFF0000u);
-                acc0[0] = fmaf(pp.x, va, acc0[0]);
-                acc0[1] = fmaf(pp.x, vb2, acc0[1]);
-                acc0[2] = fmaf(pp.x, vc, acc0[2]);
-                acc0[3] = fmaf(pp.x, vd, acc0[3]);
-                acc1[0] = fmaf(pp.y, va, acc1[0]);
-                acc1[1] = fmaf(pp.y, vb2, acc1[1]);
-                acc1[2] = fmaf(pp.y, vc, acc1[2]);
-                acc1[3] = fmaf(pp.y, vd, acc1[3]);
+                ptx::fma_x2(acc0[0], acc0[1], pp.x, pp.y, va, vb2, acc0[0], acc0[1]);
+                ptx::fma_x2(acc0[2], acc0[3], pp.x, pp.y, vc, vd, acc0[2], acc0[3]);
+                ptx::fma_x2(acc1[0], acc1[1], pp.z, pp.w, va, vb2, acc1[0], acc1[1]);
+                ptx::fma_x2(acc1[2], acc1[3], pp.z, pp.w, vc, vd, acc1[2], acc1[3]);
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&empty[s]);
@@ -338,11 +371,9 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
             red_m[warp * 2 + lane] = m_run;
             red_l[warp * 2 + lane] = l;
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            red_acc[(warp * 2 + 0) * 128 + 4 * lane + e] = acc0[e];
-            red_acc[(warp * 2 + 1) * 128 + 4 * lane + e] = acc1[e];
-        }
+        float *racc = reinterpret_cast<float *>(stages + warp * PAGE_BYTES);  // [2][128] in the warp's own stage
+        *reinterpret_cast<float4 *>(racc + 4 * lane) = make_float4(acc0[0], acc0[1], acc0[2], acc0[3]);
+        *reinterpret_cast<float4 *>(racc + 128 + 4 * lane) = make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
     }
     __syncthreads();
     if (threadIdx.x < 128) {
@@ -357,24 +388,32 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(DecodeAttnArgs a) {
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
                 const float f = red_m[w * 2 + hh] == -INFINITY ? 0.f : exp2f(red_m[w * 2 + hh] - M);
-                o += f * red_acc[(w * 2 + hh) * 128 + d];
+                o += f * reinterpret_cast<const float *>(stages + w * PAGE_BYTES)[hh * 128 + d];
                 l += f * red_l[w * 2 + hh];
             }
-            a.part_o[(base * 2 + hh) * 128 + d] = o;
-            if (d == 0) {
-                a.part_ml[(base * 2 + hh) * 2 + 0] = M;
-                a.part_ml[(base * 2 + hh) * 2 + 1] = l;
+            if (a.max_splits == 1) {
+                // One split per row: this state is the result. (0 + o) / (0 + l) is what the combine computes from a
+                // single split (its weight is exactly 1), so both forms give the same bits.
+                a.out[((size_t)b * a.q_heads + 2 * h + hh) * kHeadDim + d] = __float2bfloat16_rn((0.f + o) / (0.f + l));
+            } else {
+                a.part_o[(base * 2 + hh) * 128 + d] = o;
+                if (d == 0) {
+                    a.part_ml[(base * 2 + hh) * 2 + 0] = M;
+                    a.part_ml[(base * 2 + hh) * 2 + 1] = l;
+                }
             }
         }
     }
 }
 
 __global__ void __launch_bounds__(128) decode_combine_kernel(DecodeAttnArgs a) {
-    ptx::griddep_wait();
-    ptx::griddep_launch();
+    // The row's length is an input of the attention kernel, which lets this kernel launch only after its own wait,
+    // so it is final here before this kernel's wait; the split states are read after it.
     const int b = blockIdx.x, qh = blockIdx.y, d = threadIdx.x;
     const int h = qh / 2, hh = qh % 2;
     const int len = a.seq_len[a.slots[b]];
+    ptx::griddep_wait();
+    ptx::griddep_launch();
     if (!decode_len_ok(a, len)) {  // the attention kernel recorded the error; the row is written as zeros
         a.out[((size_t)b * a.q_heads + qh) * kHeadDim + d] = __float2bfloat16_rn(0.f);
         return;
@@ -448,12 +487,12 @@ cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_
 
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
     constexpr int ST = 4;  // 37 KiB of shared memory a CTA, six CTAs an SM (measured faster than 8 / 12 / 16)
-    const size_t smem = ST * 8192 + (4 * 32 + 4 * 2 * 128 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
+    const size_t smem = ST * 8192 + (4 * 64 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
     static SmemOptIn opt;
     cudaError_t e = opt.set((const void *)decode_attn_kernel<ST>, (int)smem);
     if (e != cudaSuccess) return e;
     e = launch_kernel(decode_attn_kernel<ST>, dim3(a.max_splits, a.kv.kv_heads, a.B), dim3(160), smem, st, a);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || a.max_splits == 1) return e;  // a single split writes the output itself
     return launch_kernel(decode_combine_kernel, dim3(a.B, a.q_heads), dim3(128), 0, st, a);
 }
 
