@@ -105,42 +105,33 @@ struct TokenInputs {
 
 // Warp w takes tokens t0 + w, t0 + w + 4, ... of this CTA's share [t0, t1) of tile (mt, nt); this loads the NT of
 // them from the warp's i0-th on. Every load is issued for all NT tokens before any result is used.
-template <int EPI, int S, int NT>
+// PART 1 is what no kernel of a decode step after its first writes (the q/k/v tokens' positions, pages, RoPE rows
+// and norm gains), which may load before the kernel waits on the previous one; PART 2 is the rest, loaded after the
+// wait (and after PART 1); PART 3 both.
+template <int EPI, int S, int NT, int PART = 3>
 __device__ __forceinline__ void load_inputs(const DecodeGemmArgs &a, TokenInputs<NT> &in, int split, int mt, int nt,
                                             int w, int lane, int i0) {
     const int t0 = split * kBN / S, t1 = (split + 1) * kBN / S;
+    if (PART & 1) {
 #pragma unroll
-    for (int i = 0; i < NT; ++i) {
-        in.tl[i] = t0 + w + 4 * (i0 + i);
-        in.tok[i] = (in.tl[i] < t1 && nt * kBN + in.tl[i] < a.N) ? nt * kBN + in.tl[i] : -1;
+        for (int i = 0; i < NT; ++i) {
+            in.tl[i] = t0 + w + 4 * (i0 + i);
+            in.tok[i] = (in.tl[i] < t1 && nt * kBN + in.tl[i] < a.N) ? nt * kBN + in.tl[i] : -1;
+        }
     }
     const int m = mt * kBM + 4 * lane;
     if (EPI == DEC_RESID) {
+        if (!(PART & 2)) return;
 #pragma unroll
         for (int i = 0; i < NT; ++i)
             if (in.tok[i] >= 0) in.xv[i] = *reinterpret_cast<const float4 *>(a.x + (size_t)in.tok[i] * a.M + m);
         in.g = a.gain ? __ldg(reinterpret_cast<const uint2 *>(a.gain + m)) : make_uint2(0, 0);
         return;
     }
-    // The RMSNorm scale of each token's input: lane g holds the sums of squares of column groups g, g + 32, ...
-    // (added in that order), then a butterfly over the warp, which leaves the same bits in every lane.
-    {
-        float part[NT];
-#pragma unroll
-        for (int i = 0; i < NT; ++i) {
-            part[i] = 0.f;
-            if (in.tok[i] >= 0 && a.ss)
-                for (int gi = lane; gi < a.nss; gi += 32) part[i] += __ldg(a.ss + (size_t)gi * a.ss_stride + in.tok[i]);
-        }
-        if (EPI == DEC_QKV) {  // the position loads go out before the scale's reduction waits on its loads
-#pragma unroll
-            for (int i = 0; i < NT; ++i) in.pos[i] = in.tok[i] >= 0 ? __ldg(a.qkv.tok_pos + in.tok[i]) : 0;
-        }
-#pragma unroll
-        for (int i = 0; i < NT; ++i) in.r[i] = a.ss ? rsqrtf(warp_sum(part[i]) / a.hidden + a.eps) : 1.f;
-    }
-    if (EPI == DEC_QKV) {
+    if (EPI == DEC_QKV && (PART & 1)) {
         const QkvEpilogue &E = a.qkv;
+#pragma unroll
+        for (int i = 0; i < NT; ++i) in.pos[i] = in.tok[i] >= 0 ? __ldg(E.tok_pos + in.tok[i]) : 0;
         const int hr = mt;
         const bool is_q = hr < E.q_heads, is_k = !is_q && hr < E.q_heads + E.kv_heads;
         if (!is_q) {
@@ -162,14 +153,25 @@ __device__ __forceinline__ void load_inputs(const DecodeGemmArgs &a, TokenInputs
             }
         }
     }
+    // The RMSNorm scale of each token's input: lane g holds the sums of squares of column groups g, g + 32, ...
+    // (added in that order), then a butterfly over the warp, which leaves the same bits in every lane.
+    if (PART & 2) {
+        float part[NT];
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+            part[i] = 0.f;
+            if (in.tok[i] >= 0 && a.ss)
+                for (int gi = lane; gi < a.nss; gi += 32) part[i] += __ldg(a.ss + (size_t)gi * a.ss_stride + in.tok[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < NT; ++i) in.r[i] = a.ss ? rsqrtf(warp_sum(part[i]) / a.hidden + a.eps) : 1.f;
+    }
 }
 
 // The cluster reduction of the same NT tokens (the S CTAs' staged accumulators, remote loads all in flight at
 // once, summed in split order) and the epilogue, lane l holding rows 4l..4l+3 of each token.
-template <int EPI, int S, int NT>
-__device__ __forceinline__ void reduce_finish(const DecodeGemmArgs &a, const TokenInputs<NT> &in, const float *stg,
-                                              int mt, int lane) {
-    float4 y[NT];
+template <int S, int NT>
+__device__ __forceinline__ void reduce_tokens(const TokenInputs<NT> &in, const float *stg, int lane, float4 (&y)[NT]) {
     {
         float4 z[NT][S];
 #pragma unroll
@@ -191,6 +193,11 @@ __device__ __forceinline__ void reduce_finish(const DecodeGemmArgs &a, const Tok
             }
         }
     }
+}
+
+template <int EPI, int NT>
+__device__ __forceinline__ void finish_tokens(const DecodeGemmArgs &a, const TokenInputs<NT> &in,
+                                              const float4 (&y)[NT], int mt, int lane) {
     const int m = mt * kBM + 4 * lane;
     if (EPI == DEC_RESID) {
 #pragma unroll
@@ -349,10 +356,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         __syncwarp();
     } else {
-        // Epilogue warps. The outputs and the norm inputs belong to the previous kernel until it completes, so wait
-        // for it, then fetch this warp's first tokens' inputs while the tensor cores work.
+        // Epilogue warps. What no kernel of the decode step after its first writes (load_inputs PART 1) loads before
+        // the wait; the outputs and the norm inputs belong to the previous kernel until it completes, so the rest of
+        // this warp's first tokens' inputs loads after it, while the tensor cores work.
+        load_inputs<EPI, S, CH, 1>(args, in, split, mt, nt, warp - 2, lane, 0);
         ptx::griddep_wait();
-        load_inputs<EPI, S, CH>(args, in, split, mt, nt, warp - 2, lane, 0);
+        load_inputs<EPI, S, CH, 2>(args, in, split, mt, nt, warp - 2, lane, 0);
         // TMEM lane quarter q = warp % 4 holds tile rows 32q..32q+31, one row a thread, 64 token columns.
         const int q = warp & 3;
         const bool ok = ptx::mbar_wait(acc_full, 0, err, 0x4004);
@@ -370,15 +379,32 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     ptx::tc_fence_before();
     ptx::cluster_sync();  // every CTA's accumulator is in its shared memory
 
+    // A thread arrives at the second cluster barrier once it has read all it needs of the other CTAs' shared memory,
+    // and waits on it just before exiting: no CTA exits while another may still read its shared memory, and the
+    // barrier's latency overlaps the epilogue's stores.
     if (warp >= 2) {
-        reduce_finish<EPI, S, CH>(args, in, stg, mt, lane);
-        for (int i0 = CH; i0 < NT; i0 += CH) {  // tokens beyond the first CH of the warp (S below 4)
-            load_inputs<EPI, S, CH>(args, in, split, mt, nt, warp - 2, lane, i0);
-            reduce_finish<EPI, S, CH>(args, in, stg, mt, lane);
+        if (NT <= CH) {
+            float4 y[CH];
+            reduce_tokens<S, CH>(in, stg, lane, y);
+            __syncwarp();
+            ptx::cluster_arrive();
+            finish_tokens<EPI, CH>(args, in, y, mt, lane);
+        } else {  // tokens beyond the first CH of the warp (S below 4)
+            for (int i0 = 0; i0 < NT; i0 += CH) {
+                if (i0 > 0) load_inputs<EPI, S, CH>(args, in, split, mt, nt, warp - 2, lane, i0);
+                float4 y[CH];
+                reduce_tokens<S, CH>(in, stg, lane, y);
+                finish_tokens<EPI, CH>(args, in, y, mt, lane);
+            }
+            __syncwarp();
+            ptx::cluster_arrive();
         }
+    } else {
+        __syncwarp();
+        ptx::cluster_arrive();
     }
     __syncwarp();
-    ptx::cluster_sync();  // no CTA exits while another may still read its shared memory
+    ptx::cluster_wait();
     ptx::tc_fence_after();
     if (warp == 1) ptx::tmem_dealloc(tmem, kBN);
 }
