@@ -93,6 +93,21 @@ __device__ __forceinline__ void bulk_load(void *smem, const void *gmem, uint32_t
         : "memory");
 }
 
+// The same with an L2 cache policy (createpolicy), e.g. evict-first for data read once.
+__device__ __forceinline__ void bulk_load_hint(void *smem, const void *gmem, uint32_t bytes, uint64_t *bar,
+                                               uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(smem)),
+        "l"((uint64_t)gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // ---- tcgen05 -----------------------------------------------------------------------------------------------------
 
 // Allocates `cols` TMEM columns (a power of two >= 32) for the CTA; one whole warp executes it. The address lands in

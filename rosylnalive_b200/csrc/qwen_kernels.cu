@@ -242,9 +242,9 @@ __global__ void __launch_bounds__(160, 6) decode_attn_kernel(DecodeAttnArgs a) {
                 const int page = __shfl_sync(FULL, pg, j);
                 if (lane == 0) {
                     ptx::mbar_arrive_expect_tx(&full[j], PAGE_BYTES);
-                    ptx::bulk_load(stages + j * PAGE_BYTES,
-                                   a.kv.pool + (size_t)page * page_elems + (size_t)h * 2 * kPageTokens * kHeadDim,
-                                   PAGE_BYTES, &full[j]);
+                    ptx::bulk_load_hint(stages + j * PAGE_BYTES,
+                                        a.kv.pool + (size_t)page * page_elems + (size_t)h * 2 * kPageTokens * kHeadDim,
+                                        PAGE_BYTES, &full[j], ptx::policy_evict_first());
                 }
             }
         }
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(160, 6) decode_attn_kernel(DecodeAttnArgs a) {
                     const __nv_bfloat16 *src =
                         a.kv.pool + (size_t)page * page_elems + (size_t)h * 2 * kPageTokens * kHeadDim;
                     ptx::mbar_arrive_expect_tx(&full[s], PAGE_BYTES);
-                    ptx::bulk_load(stages + s * PAGE_BYTES, src, PAGE_BYTES, &full[s]);
+                    ptx::bulk_load_hint(stages + s * PAGE_BYTES, src, PAGE_BYTES, &full[s], ptx::policy_evict_first());
                 }
             }
             if (!__shfl_sync(FULL, ok, 0)) break;
