@@ -316,10 +316,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
     if (warp == 0) {
         if (ptx::elect_one()) {
+            const uint64_t wpol = ptx::policy_evict_first();  // each weight byte is read once a step
             const int pre = min(kStages, nk);
             for (int j = 0; j < pre; ++j) {  // the weights: no earlier kernel writes them
                 ptx::mbar_arrive_expect_tx(&full[j], kStageBytes);
-                ptx::tma_load_2d(smem + j * kStageBytes, &tmap_a, &full[j], (k0 + j) * kBK, mt * kBM);
+                ptx::tma_load_2d_hint(smem + j * kStageBytes, &tmap_a, &full[j], (k0 + j) * kBK, mt * kBM, wpol);
             }
             ptx::griddep_wait();  // the tokens' activations come from the previous kernel
             int j = 0;
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 if (j >= pre) {
                     if (!ptx::mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1, err, 0x4001)) break;
                     ptx::mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    ptx::tma_load_2d(sa, &tmap_a, &full[s], (k0 + j) * kBK, mt * kBM);
+                    ptx::tma_load_2d_hint(sa, &tmap_a, &full[s], (k0 + j) * kBK, mt * kBM, wpol);
                 }
                 ptx::tma_load_2d(sa + kABytes, &tmap_b, &full[s], (k0 + j) * kBK, nt * kBN);
             }

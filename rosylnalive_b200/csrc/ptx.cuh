@@ -84,6 +84,16 @@ __device__ __forceinline__ void tma_load_2d(void *smem, const CUtensorMap *map, 
         : "memory");
 }
 
+// tma_load_2d with an L2 cache policy (createpolicy), e.g. evict-first for data read once.
+__device__ __forceinline__ void tma_load_2d_hint(void *smem, const CUtensorMap *map, uint64_t *bar, int32_t x,
+                                                 int32_t y, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%3, %4}], [%2], %5;" ::"r"(smem_u32(smem)),
+        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
 // 1D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16), completing tx bytes on `bar`.
 __device__ __forceinline__ void bulk_load(void *smem, const void *gmem, uint32_t bytes, uint64_t *bar) {
     asm volatile(
