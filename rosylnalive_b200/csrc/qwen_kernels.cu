@@ -96,22 +96,35 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *logits, int V,
     __shared__ __align__(16) float part[4];  // this CTA's (value, index, NaN seen) for rank 0
     const int rank = blockIdx.x;             // the cluster rank: clusters of kArgmaxCtas along x
     const float *row = logits + (size_t)blockIdx.y * V;
-    const int chunk = (V + kArgmaxCtas - 1) / kArgmaxCtas;
-    const int c0 = rank * chunk, c1 = min(V, c0 + chunk);
+    // A multiple of 4 columns a CTA, so that with V a multiple of 4 every row and chunk starts 16-byte aligned and the
+    // scan reads float4s (each thread's elements in increasing index order, as the scalar scan).
+    const int chunk = ((V + kArgmaxCtas - 1) / kArgmaxCtas + 3) & ~3;
+    const int c0 = min(V, rank * chunk), c1 = min(V, c0 + chunk);
     if (threadIdx.x == 0) nan_any = 0;
     __syncthreads();
     float best = -INFINITY;
     int idx = -1;
     bool nan = false;
-#pragma unroll 4
-    for (int c = c0 + threadIdx.x; c < c1; c += 256) {
-        const float v = row[c];
+    auto take = [&](float v, int c) {
         if (isnan(v))
             nan = true;
         else if (idx < 0 || v > best) {
             best = v;
             idx = c;
         }
+    };
+    if ((V & 3) == 0) {
+#pragma unroll 4
+        for (int c = c0 + 4 * (int)threadIdx.x; c < c1; c += 1024) {
+            const float4 v = *reinterpret_cast<const float4 *>(row + c);
+            take(v.x, c);
+            take(v.y, c + 1);
+            take(v.z, c + 2);
+            take(v.w, c + 3);
+        }
+    } else {
+#pragma unroll 4
+        for (int c = c0 + threadIdx.x; c < c1; c += 256) take(row[c], c);
     }
     if (nan) nan_any = 1;
 #pragma unroll
