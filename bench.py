@@ -57,6 +57,9 @@ def parse():
     p.add_argument("--microbatches", type=int, default=2, help="--pipeline: sequence groups in flight")
     p.add_argument("--op-bench", action="store_true",
                    help="operator benchmarks only (config 2 attention, config 4 GEMM shapes); one JSON line")
+    p.add_argument("--attention-libraries", action="store_true",
+                   help="--op-bench: also time the config-2 prefill through the attention libraries in the image "
+                        "(flash_attn, flashinfer's Blackwell backends; the CUTLASS one compiles for about 2 minutes)")
     return p.parse_args()
 
 
@@ -472,7 +475,7 @@ def prefill_bench(eng, cfg, dist, pk, stream, timed, batch=16, L=2048):
                          "note": "whole prefill (GEMMs + attention) against the measured bf16 GEMM peak"}}
 
 
-def op_bench():
+def op_bench(libraries=False):
     """Operator benchmarks on cuda:0 through the C ABI (one JSON line; not the headline): BASELINE config 2 (the
     standalone GQA attention op: batch 8, 16 query / 8 KV heads, head_dim 128, causal prefill of 2048 tokens and
     decode of one token over 4096 cached ones, bf16 Q/K/V ~ N(0, 1)) and the four prefill GEMM shapes of config 4
@@ -518,6 +521,8 @@ def op_bench():
     res["attention_prefill"] = {"shape": "8 x 2048, 16/8 heads, causal", "ms": ms,
                                 "tflops": flops / ms / 1e9, "frac_of_bf16_peak": flops / ms / 1e9 / pk["bf16_tflops"],
                                 "flops": flops, "note": "causal FLOPs 4*d*heads*sum(L(L+1)/2)"}
+    if libraries:
+        res["attention_prefill_libraries"] = library_attention(q, k, v, cu, L, QH, KVH, flops, med_ms)
     # config 2, decode: one query per sequence over 4096 cached tokens in 16-token pages
     C = 4096
     pages = C // 16
@@ -563,10 +568,43 @@ def op_bench():
     print(json.dumps(res), flush=True)
 
 
+def library_attention(q, k, v, cu, L, QH, KVH, flops, med_ms):
+    """The same config-2 causal prefill through the attention libraries in the image, for comparison only (they are
+    not part of this backend): flash_attn's varlen kernel and flashinfer's ragged prefill on its Blackwell backends.
+    A backend that does not build or run here reports why."""
+    import torch
+
+    out = {}
+    scale = 1.0 / 128 ** 0.5
+    try:
+        from flash_attn import flash_attn_varlen_func
+
+        ms = med_ms(lambda: flash_attn_varlen_func(q, k, v, cu, cu, L, L, softmax_scale=scale, causal=True))
+        out["flash_attn_varlen"] = {"ms": ms, "tflops": flops / ms / 1e9}
+    except Exception as e:  # noqa: BLE001 - report any failure of an optional comparison
+        out["flash_attn_varlen"] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+    try:
+        import flashinfer
+    except Exception as e:  # noqa: BLE001
+        out["flashinfer"] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+        return out
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for backend in ("cutlass", "cute-dsl", "fa2"):
+        try:
+            w = flashinfer.BatchPrefillWithRaggedKVCacheWrapper(ws, "NHD", backend=backend)
+            w.plan(cu, cu, QH, KVH, 128, causal=True, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+                   sm_scale=scale)
+            ms = med_ms(lambda: w.run(q, k, v))
+            out[f"flashinfer_{backend}"] = {"ms": ms, "tflops": flops / ms / 1e9}
+        except Exception as e:  # noqa: BLE001
+            out[f"flashinfer_{backend}"] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+    return out
+
+
 def main():
     args = parse()
     if args.op_bench:
-        op_bench()
+        op_bench(libraries=args.attention_libraries)
         return
     dist = Dist()
     if args.impl == "reference":
