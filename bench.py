@@ -523,6 +523,8 @@ def op_bench(libraries=False):
                                 "flops": flops, "note": "causal FLOPs 4*d*heads*sum(L(L+1)/2)"}
     if libraries:
         res["attention_prefill_libraries"] = library_attention(q, k, v, cu, L, QH, KVH, flops, med_ms)
+        del q, k, v, out
+        res["attention_decode_config5_libraries"] = library_decode(QH, KVH, med_ms, pk, g)
     # config 2, decode: one query per sequence over 4096 cached tokens in 16-token pages
     C = 4096
     pages = C // 16
@@ -599,6 +601,50 @@ def library_attention(q, k, v, cu, L, QH, KVH, flops, med_ms):
         except Exception as e:  # noqa: BLE001
             out[f"flashinfer_{backend}"] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
     return out
+
+
+def library_decode(QH, KVH, med_ms, pk, g):
+    """Decode attention at the config-5 shape (64 sequences, 4096 cached tokens in 16-token pages, one query each):
+    this backend's operator (32 pages a split, as the engine) beside flashinfer's paged decode on the same pages,
+    copied into its [page][K/V][kv head][16][128] layout. For comparison only."""
+    import torch
+
+    from rosylnalive_b200 import ops
+
+    B, C, P = 64, 4096, 16
+    pages = C // P
+    nbytes = B * C * KVH * 2 * 128 * 2 + 2 * B * QH * 128 * 2
+    pool = torch.randn(B * pages, KVH, 2, P, 128, device="cuda", generator=g).to(torch.bfloat16)
+    table = torch.randperm(B * pages, device="cuda", generator=g).to(torch.int32).view(B, pages)
+    lens = torch.full((B,), C, dtype=torch.int32, device="cuda")
+    slots = torch.arange(B, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, QH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(B, QH, 128, device="cuda", dtype=torch.bfloat16)
+    ws = torch.empty(ops.decode_attention_workspace(B, KVH, pages, 32) // 4, device="cuda")
+    res = {"shape": "64 x 1 query over 4096 cached tokens, 16/8 heads, 16-token pages", "bytes": nbytes}
+    ms = med_ms(lambda: ops.decode_attention(q, pool, table, lens, slots, out, ws, 32, 1.0 / 128 ** 0.5))
+    res["ours"] = {"ms": ms, "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / pk["hbm_gbs"]}
+    try:
+        import flashinfer
+    except Exception as e:  # noqa: BLE001 - report any failure of an optional comparison
+        res["flashinfer"] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+        return res
+    cache = pool.permute(0, 2, 1, 3, 4).contiguous()  # [page][K/V][kv head][16][128]
+    indptr = torch.arange(0, B * pages + 1, pages, device="cuda", dtype=torch.int32)
+    indices = table.reshape(-1).contiguous()
+    last = torch.full((B,), P, dtype=torch.int32, device="cuda")
+    fws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for backend, tc in (("fa2", False), ("fa2", True), ("trtllm-gen", False)):
+        key = f"flashinfer_{backend}" + ("_tensor_cores" if tc else "")
+        try:
+            w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(fws, "HND", use_tensor_cores=tc, backend=backend)
+            w.plan(indptr, indices, last, QH, KVH, 128, P, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+                   sm_scale=1.0 / 128 ** 0.5)
+            ms = med_ms(lambda: w.run(q, cache))
+            res[key] = {"ms": ms, "gbs": nbytes / ms / 1e6}
+        except Exception as e:  # noqa: BLE001
+            res[key] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+    return res
 
 
 def main():
