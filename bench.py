@@ -624,6 +624,10 @@ def library_decode(QH, KVH, med_ms, pk, g):
     res = {"shape": "64 x 1 query over 4096 cached tokens, 16/8 heads, 16-token pages", "bytes": nbytes}
     ms = med_ms(lambda: ops.decode_attention(q, pool, table, lens, slots, out, ws, 32, 1.0 / 128 ** 0.5))
     res["ours"] = {"ms": ms, "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / pk["hbm_gbs"]}
+    # one split a row: 512 CTAs, all resident, each writing its output (no combine launch)
+    ws1 = torch.empty(ops.decode_attention_workspace(B, KVH, pages, pages) // 4, device="cuda")
+    ms = med_ms(lambda: ops.decode_attention(q, pool, table, lens, slots, out, ws1, pages, 1.0 / 128 ** 0.5))
+    res["ours_one_split"] = {"ms": ms, "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / pk["hbm_gbs"]}
     try:
         import flashinfer
     except Exception as e:  # noqa: BLE001 - report any failure of an optional comparison
