@@ -6,7 +6,8 @@
 // one thread-block cluster, and instead of writing fp32 partials for another kernel to add up, they reduce through
 // distributed shared memory:
 //   warp 0      TMA producer: the CTA's weight k-blocks are requested before the kernel waits for the previous one
-//               (programmatic dependent launch; the weights are written by no kernel), then the token k-blocks;
+//               (programmatic dependent launch; the weights are written by no kernel), L2 evict-first (each weight
+//               byte is read once a step), then the token k-blocks;
 //   warp 1      TMEM allocation (64 columns) and one thread issuing tcgen05.mma M=128, N=64, K=16;
 //   warps 2..5  the epilogue: each thread moves its accumulator row (TMEM lane) into the CTA's shared memory as
 //               [token][row], the cluster synchronises, and every CTA then sums one share of the tile's tokens over

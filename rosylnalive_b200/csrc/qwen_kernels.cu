@@ -177,7 +177,8 @@ __global__ void advance_kernel(const int32_t *slots, int B, int32_t *seq_len, in
 // ---- paged split-K decode attention -----------------------------------------------------------------------------
 //
 // CTA = (split, kv head h, batch row b): the pages [split * PPS, ...) of sequence slots[b]. Warp 4 streams each page's
-// K+V block of head h (8 KiB contiguous) into a ring of ST shared-memory stages with cp.async.bulk; consumer warp w
+// K+V block of head h (8 KiB contiguous) into a ring of ST shared-memory stages with cp.async.bulk, L2 evict-first
+// (every cached byte is read once a step, so the step's other data keeps its place in L2); consumer warp w
 // (0..3) handles the pages w, w + 4, ... of the split with its own online softmax for the two q heads 2h, 2h + 1:
 //   scores: lane (half = lane / 16, li = lane % 16) reads dims 8 li .. 8 li + 7 of keys 2i + half (16-byte smem
 //           loads, conflict-free), keeps 16 partial dots (8 keys x 2 heads) and a 4-step shuffle reduce-scatter
