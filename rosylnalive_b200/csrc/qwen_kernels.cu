@@ -500,7 +500,7 @@ cudaError_t launch_advance(const int32_t *slots, int B, int32_t *seq_len, int32_
 }
 
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, cudaStream_t st) {
-    constexpr int ST = 4;  // 37 KiB of shared memory a CTA, six CTAs an SM (measured faster than 8 / 12 / 16)
+    constexpr int ST = 4;  // 34 KiB of shared memory a CTA, six CTAs an SM (measured faster than 8 / 12 / 16)
     const size_t smem = ST * 8192 + (4 * 64 + 16) * sizeof(float) + 2 * ST * sizeof(uint64_t);
     static SmemOptIn opt;
     cudaError_t e = opt.set((const void *)decode_attn_kernel<ST>, (int)smem);
