@@ -248,7 +248,8 @@ lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d
  * of a page and head, 8 KiB), page_table int32 [seqs][pages_per_seq], seq_len int32 [seqs] (keys per sequence,
  * the new one included), slots int32 [batch] (device). q/out bf16 [batch][q_heads][128]; q_heads = 2 kv_heads.
  * Each CTA streams pages_per_split pages of one (row, kv head); the splits' partial softmax states go to
- * `workspace` (lrm_op_decode_attention_workspace bytes, 16-byte aligned) and a second kernel merges them. */
+ * `workspace` (lrm_op_decode_attention_workspace bytes, 16-byte aligned) and a second kernel merges them; with one
+ * split a row (pages_per_split >= pages_per_seq) the attention kernel writes the output itself. */
 typedef struct lrm_decode_attn_desc {
     uint64_t q, pool, page_table, seq_len, slots, out, workspace;
     int32_t batch, q_heads, kv_heads, head_dim, pages_per_seq, pages_per_split;
