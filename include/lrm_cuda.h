@@ -179,6 +179,12 @@ lrm_status lrm_op_error_word(uint32_t *code, int32_t clear);
  * (src/Lrm.Gpu.D3D12/Backend.fs:109, Context.fs:200-234), without hanging or faulting a GPU. */
 lrm_status lrm_op_wait_probe(void *stream, uint32_t polls, uint32_t code);
 
+/* The engine's greedy pick as an operator: out[r] = the lowest index of the maximum of row r of logits (fp32
+ * [rows][vocab], device; 16-byte aligned when vocab is a multiple of 4, which the kernel then reads as float4), or
+ * 0xFFFFFFFF for a row holding a NaN: the argmax_rows contract (src/Lrm.Tensor.CpuReference/CpuRef.fs:452-466).
+ * A row is scanned by a cluster of 8 CTAs; rows is at most 65535. */
+lrm_status lrm_op_argmax_rows(void *stream, const float *logits, int32_t rows, int32_t vocab, uint32_t *out);
+
 #define LRM_GEMM_F32 0     /* out_f32[m, n] = acc */
 #define LRM_GEMM_RESID 1   /* out_f32[m, n] = resid[m, n] + acc (resid may equal out) */
 #define LRM_GEMM_SWIGLU 2  /* b rows interleave gate/up in blocks of 64; out_bf16[m, n/2] = silu(gate) * up */

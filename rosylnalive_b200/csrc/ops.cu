@@ -181,6 +181,14 @@ lrm_status lrm_op_wait_probe(void *stream, uint32_t polls, uint32_t code) {
     return op_cuda(cudaGetLastError(), "wait probe");
 }
 
+lrm_status lrm_op_argmax_rows(void *stream, const float *logits, int32_t rows, int32_t vocab, uint32_t *out) {
+    if (!logits || !out) return op_fail(LRM_ERR_ARGUMENT, "argmax: null pointer");
+    if (rows < 1 || rows > 65535 || vocab < 1) return op_fail(LRM_ERR_ARGUMENT, "argmax: rows must be 1 .. 65535");
+    if (vocab % 4 == 0 && ((uintptr_t)logits & 15))
+        return op_fail(LRM_ERR_ARGUMENT, "argmax: logits must be 16-byte aligned when vocab is a multiple of 4");
+    return op_cuda(launch_argmax(logits, rows, vocab, out, (cudaStream_t)stream), "argmax");
+}
+
 uint64_t lrm_op_decode_attention_workspace(int32_t batch, int32_t kv_heads, int32_t pages_per_seq,
                                            int32_t pages_per_split) {
     if (batch < 1 || kv_heads < 1 || pages_per_seq < 1 || pages_per_split < 1) return 0;

@@ -49,6 +49,7 @@ N.extra_signatures({
     "lrm_op_decode_attention": [P, ctypes.POINTER(DecodeAttnDesc)],
     "lrm_op_decode_attention_static": [P, ctypes.POINTER(DecodeAttnDesc)],
     "lrm_op_wait_probe": [P, U32, U32],
+    "lrm_op_argmax_rows": [P, P, I32, I32, P],
     "lrm_op_decode_gemm": [P, ctypes.POINTER(DecodeGemmDesc)],
 }, {"lrm_op_decode_attention_workspace": U64})
 
@@ -71,6 +72,13 @@ def error_word(clear: bool = True) -> int:
     v = ctypes.c_uint32()
     N.check(N.lib().lrm_op_error_word(ctypes.byref(v), 1 if clear else 0), None, "error_word")
     return v.value
+
+
+def argmax_rows(logits, out, stream=None):
+    """out[r] (uint32 as int32 storage) = the lowest index of the maximum of logits[r] (fp32 [rows, vocab] on the
+    device), or 0xFFFFFFFF for a row holding a NaN: the engine's greedy pick."""
+    N.check(N.lib().lrm_op_argmax_rows(_stream(stream), ctypes.c_void_p(logits.data_ptr()), logits.shape[0],
+                                       logits.shape[1], ctypes.c_void_p(out.data_ptr())), None, "argmax_rows")
 
 
 def wait_probe(polls: int, code: int, stream=None):
