@@ -565,7 +565,9 @@ extern "C" lrm_status lrm_op_decode_gemm(void *stream, const lrm_decode_gemm_des
     if (!d) return op_fail(LRM_ERR_ARGUMENT, "decode gemm: descriptor is null");
     if (d->epilogue != LRM_DEC_RESID && d->epilogue != LRM_DEC_SWIGLU)
         return op_fail(LRM_ERR_ARGUMENT, "decode gemm: the epilogue must be LRM_DEC_RESID or LRM_DEC_SWIGLU");
-    if (d->m < 1 || d->n < 1 || d->k < 1) return op_fail(LRM_ERR_ARGUMENT, "decode gemm: sizes must be positive");
+    // the tile and k-block counts are int32 ((k + 63) / 64 and the like): a bound well below INT_MAX
+    if (d->m < 1 || d->n < 1 || d->k < 1 || d->m > (1 << 30) || d->n > (1 << 30) || d->k > (1 << 30))
+        return op_fail(LRM_ERR_ARGUMENT, "decode gemm: sizes must be 1 .. 2^30");
     DecodeGemmArgs a;
     memset(&a, 0, sizeof a);
     a.M = d->m;

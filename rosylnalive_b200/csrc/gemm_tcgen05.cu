@@ -1141,7 +1141,9 @@ bool gemm_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t col
 }
 
 const char *gemm_check(const GemmArgs &a) {
-    if (a.M < 1 || a.N < 1 || a.K < 1) return "M, N and K must be positive";
+    // tile and k-block counts are int32 ((K + 63) / 64 and the like): a bound well below INT_MAX
+    if (a.M < 1 || a.N < 1 || a.K < 1 || a.M > (1 << 30) || a.N > (1 << 30) || a.K > (1 << 30))
+        return "M, N and K must be 1 .. 2^30";
     if (a.K % 8) return "K must be a multiple of 8 (16-byte rows for TMA)";
     if (((uintptr_t)a.A & 15) || ((uintptr_t)a.B & 15)) return "A and B must be 16-byte aligned";
     if (a.bn != 64 && a.bn != 128 && a.bn != 256) return "bn must be 64, 128 or 256";

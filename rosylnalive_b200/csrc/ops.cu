@@ -113,6 +113,8 @@ lrm_status lrm_op_error_word(uint32_t *code, int32_t clear) {
 
 lrm_status lrm_op_gemm_bf16(void *stream, const lrm_gemm_desc *d) {
     if (!d) return op_fail(LRM_ERR_ARGUMENT, "descriptor is null");
+    if (d->m < 1 || d->n < 1 || d->k < 1 || d->m > (1 << 30) || d->n > (1 << 30) || d->k > (1 << 30))
+        return op_fail(LRM_ERR_ARGUMENT, "gemm: M, N and K must be 1 .. 2^30");
     GemmArgs a;
     memset(&a, 0, sizeof a);
     a.M = d->m;
@@ -183,7 +185,9 @@ lrm_status lrm_op_wait_probe(void *stream, uint32_t polls, uint32_t code) {
 
 lrm_status lrm_op_argmax_rows(void *stream, const float *logits, int32_t rows, int32_t vocab, uint32_t *out) {
     if (!logits || !out) return op_fail(LRM_ERR_ARGUMENT, "argmax: null pointer");
-    if (rows < 1 || rows > 65535 || vocab < 1) return op_fail(LRM_ERR_ARGUMENT, "argmax: rows must be 1 .. 65535");
+    if (rows < 1 || rows > 65535) return op_fail(LRM_ERR_ARGUMENT, "argmax: rows must be 1 .. 65535");
+    // the kernel's column arithmetic (chunk rounding, strides of 1024) is int32: a bound well below INT_MAX
+    if (vocab < 1 || vocab > (1 << 30)) return op_fail(LRM_ERR_ARGUMENT, "argmax: vocab must be 1 .. 2^30");
     if (vocab % 4 == 0 && ((uintptr_t)logits & 15))
         return op_fail(LRM_ERR_ARGUMENT, "argmax: logits must be 16-byte aligned when vocab is a multiple of 4");
     return op_cuda(launch_argmax(logits, rows, vocab, out, (cudaStream_t)stream), "argmax");

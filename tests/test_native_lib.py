@@ -79,3 +79,21 @@ def test_device_info_layout_matches_the_raw_binding():
     want = {"index": 0, "name": 4, "vendor_id": 260, "pci_device_id": 264, "driver": 268, "memory_bytes": 336,
             "sm_count": 344, "cc_major": 348, "cc_minor": 352, "accepted": 356, "rejection": 360}
     assert {k: getattr(C, k).offset for k in want} == want
+
+
+def test_operators_refuse_sizes_past_their_int32_bound():
+    # Each check returns before any CUDA call, so this runs without a GPU; the pointers are never dereferenced.
+    import ctypes
+
+    from rosylnalive_b200 import ops as O
+
+    fake = ctypes.c_void_p(0x10000)
+    big = (1 << 30) + 1
+    assert N.lib().lrm_op_argmax_rows(None, fake, 1, big, fake) == N.LRM_ERR_ARGUMENT
+    assert N.lib().lrm_op_argmax_rows(None, fake, 1, 0, fake) == N.LRM_ERR_ARGUMENT
+    d = O.DecodeGemmDesc(m=128, n=64, k=big, w=0x10000, b=0x10000, epilogue=O.DEC_RESID)
+    assert N.lib().lrm_op_decode_gemm(None, ctypes.byref(d)) == N.LRM_ERR_ARGUMENT
+    d.k, d.m = 1024, big
+    assert N.lib().lrm_op_decode_gemm(None, ctypes.byref(d)) == N.LRM_ERR_ARGUMENT
+    g = O.GemmDesc(m=128, n=128, k=(1 << 31) - 1, a=0x10000, b=0x10000, epilogue=O.GEMM_F32)
+    assert N.lib().lrm_op_gemm_bf16(None, ctypes.byref(g)) == N.LRM_ERR_ARGUMENT
