@@ -167,9 +167,11 @@ lrm_status lrm_cuda_timer_end(lrm_cmdlist list, uint32_t timer_id);
 lrm_status lrm_op_set_device(int32_t device);
 
 /* Reads the current device's error word (0 = no kernel reported an error); clears it when `clear` != 0. Codes:
- * 0x1xxx, 0x2001-0x2003, 0x3xxx a bounded wait that gave up (GEMM, decode attention, prefill attention);
+ * 0x1xxx, 0x2001-0x2003, 0x3001-0x3009 a bounded wait that gave up (GEMM, decode attention, prefill attention);
  * 0x2010 a decode-attention row whose seq_len is below 1 or needs more pages than its page-table row (the row is
- * not read and its output is zeros). */
+ * not read and its output is zeros); 0x3010 a prefill-attention sequence whose cu_seqlens rows fall outside
+ * total_tokens or exceed max_len, or whose cached-token count is negative (the sequence is not computed and its
+ * output rows are left unwritten). */
 lrm_status lrm_op_error_word(uint32_t *code, int32_t clear);
 
 /* Runs one kernel whose bounded in-kernel wait can never complete (an mbarrier nothing arrives on), with a limit of

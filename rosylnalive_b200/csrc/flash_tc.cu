@@ -55,6 +55,7 @@ struct FlashTcParams {
     // paged K/V (paged != 0): page table [slots][pages_per_seq], each sequence's slot and cached tokens before it
     const int32_t *pages, *seq_slot, *past;
     int pages_per_seq, paged;
+    int total_tokens;  // rows of q and out: every sequence must lie inside them
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -95,9 +96,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int start = p.cu_seqlens[seq];
     const int len = p.cu_seqlens[seq + 1] - start;
     const int q0 = qt * TQ;
+    const int past = p.paged ? p.past[seq] : 0;  // row r of the chunk is position past + r
+    // cu_seqlens and past live in device memory, so the host cannot check them: a sequence outside the q/out rows,
+    // longer than max_len, or with negative cached tokens is not computed (its rows are left as they were) and
+    // one CTA of it records the code. Whole CTA, before any barrier, TMEM use or copy.
+    if (start < 0 || len < 0 || len > p.max_len || start > p.total_tokens - len || past < 0) {
+        if (blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0) atomicCAS(p.err, 0u, kErrPrefillSeq);
+        return;
+    }
     if (q0 >= len) return;  // whole CTA, before any barrier or TMEM use
     const int kvh = h0 / (p.q_heads / p.kv_heads);
-    const int past = p.paged ? p.past[seq] : 0;  // row r of the chunk is position past + r
     const int n_kt = (past + min(len, q0 + TQ) - 1) / TK + 1;
 
     extern __shared__ uint8_t smem_raw[];
@@ -472,6 +480,7 @@ cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_toke
     p.seq_slot = a.seq_slot;
     p.past = a.past;
     p.pages_per_seq = a.pages_per_seq;
+    p.total_tokens = total_tokens;
     dim3 grid(a.q_heads / p.heads_per_cta, a.nseq, (a.max_len + TQ - 1) / TQ);
     return launch_kernel(flash_tc_kernel, grid, dim3(kThreads), SMEM_BYTES, st, tq, tk, tv, p);
 }

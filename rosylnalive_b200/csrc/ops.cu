@@ -154,6 +154,8 @@ lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d
     if (!d->q || !d->k || !d->v || !d->out || !d->cu_seqlens || ((d->q | d->k | d->v | d->out) & 15))
         return op_fail(LRM_ERR_ARGUMENT, "prefill attention: pointers must be non-null and 16-byte aligned");
     if (d->total_tokens < 1) return op_fail(LRM_ERR_ARGUMENT, "prefill attention: total_tokens must be positive");
+    if (d->max_len > 65535 * 128)  // one grid z index per 128-row query tile
+        return op_fail(LRM_ERR_ARGUMENT, "prefill attention: max_len must be at most 65535 * 128");
     uint32_t *err = device_error_word();
     if (!err) return LRM_ERR_CUDA;
     PrefillAttnArgs a;

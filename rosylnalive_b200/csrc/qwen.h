@@ -66,6 +66,9 @@ struct PrefillAttnArgs {
     const int32_t *pages = nullptr, *seq_slot = nullptr, *past = nullptr;
     int pages_per_seq = 0, kv_pages = 0;
 };
+// A prefill sequence whose rows fall outside total_tokens, longer than max_len, or with past < 0 is not computed:
+// the kernel writes kErrPrefillSeq into err and leaves its output rows unwritten.
+constexpr uint32_t kErrPrefillSeq = 0x3010;
 // Runs on tcgen05 tensor cores (TMA tiles, TMEM accumulators); total_tokens = rows of q/k/v.
 cudaError_t launch_prefill_attention_tc(const PrefillAttnArgs &a, int total_tokens, uint32_t *err, cudaStream_t st);
 

@@ -325,6 +325,10 @@ static lrm_status sync_check(lrm_qwen Q) {
             snprintf(buf, sizeof buf, "decode attention: a row's key count exceeds its page table (code 0x%x)", code);
             return qfail(Q, LRM_ERR_STATE, buf);
         }
+        if (code == kErrPrefillSeq) {
+            snprintf(buf, sizeof buf, "prefill attention: a sequence lies outside its rows (code 0x%x)", code);
+            return qfail(Q, LRM_ERR_STATE, buf);
+        }
         snprintf(buf, sizeof buf, "a kernel's bounded wait gave up (code 0x%x)", code);
         return qfail(Q, LRM_ERR_TIMEOUT, buf);
     }

@@ -169,3 +169,32 @@ def test_decode_attention_refuses_page_counts_above_2_20():
     assert ops.decode_attention_workspace(1, 8, 1 << 20, (1 << 20) + 1) == 0
     with pytest.raises(ValueError):
         ops.decode_attention(q, pool, t, lens, lens, q, torch.empty(1 << 10, device="cuda"), (1 << 20) + 1, 0.1)
+
+
+@pytest.mark.parametrize("case", ["past_total_tokens", "longer_than_max_len"])
+def test_prefill_attention_sequence_outside_its_rows(tables, case):
+    # cu_seqlens lives on the device, so only the kernel can check it. A sequence that runs past total_tokens, or is
+    # longer than max_len, is not computed: the error word gets 0x3010, its rows stay as they were, and the other
+    # sequence is computed as usual. The buffers hold 256 rows more than total_tokens (poisoned), which stay
+    # untouched too.
+    cos, sin = tables
+    lens, slack = (100, 60), 256
+    T = sum(lens)
+    q, k, v = make_qkv(T + slack, 400, cos, sin)
+    if case == "past_total_tokens":
+        cu_host, max_len, bad, good = [0, 100, 100 + 60 + 200], 260, 1, 0
+    else:
+        cu_host, max_len, bad, good = [0, 100, 160], 64, 0, 1
+    cu = torch.tensor(cu_host, dtype=torch.int32, device="cuda")
+    qd, kd, vd = to_dev(q, (T + slack, QH, HD)), to_dev(k, (T + slack, KVH, HD)), to_dev(v, (T + slack, KVH, HD))
+    out = torch.full((T + slack, QH, HD), float("nan"), device="cuda", dtype=torch.bfloat16)
+    ops.prefill_attention(qd[:T], kd[:T], vd[:T], out[:T], cu, max_len, SCALE)
+    torch.cuda.synchronize()
+    assert ops.error_word(clear=True) == 0x3010
+    got = out.float().cpu().numpy().reshape(T + slack, QH * HD)
+    starts = (0, 100)
+    b0, b1 = starts[bad], starts[bad] + lens[bad]
+    assert np.all(np.isnan(got[b0:b1])) and np.all(np.isnan(got[T:]))
+    sl = slice(starts[good], starts[good] + lens[good])
+    r64 = O.attention(q[sl], k[sl], v[sl], QH, KVH, HD, 0, SCALE, "f64")
+    assert rel(got[sl], r64) <= 1e-2, rel(got[sl], r64)
