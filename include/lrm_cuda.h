@@ -257,7 +257,11 @@ lrm_status lrm_op_prefill_attention(void *stream, const lrm_prefill_attn_desc *d
  * the new one included), slots int32 [batch] (device). q/out bf16 [batch][q_heads][128]; q_heads = 2 kv_heads.
  * Each CTA streams pages_per_split pages of one (row, kv head); the splits' partial softmax states go to
  * `workspace` (lrm_op_decode_attention_workspace bytes, 16-byte aligned) and a second kernel merges them; with one
- * split a row (pages_per_split >= pages_per_seq) the attention kernel writes the output itself. */
+ * split a row (pages_per_split >= pages_per_seq) the attention kernel writes the output itself. The kernels check
+ * each row's seq_len against its page-table row (error word 0x2010), but not the values inside the device arrays
+ * that index memory: every slots[b] must be a row of page_table, and every page id a row reads (its first
+ * ceil(seq_len / 16) entries) a page of pool, as for any pointer the caller passes (neither count is in the
+ * descriptor). */
 typedef struct lrm_decode_attn_desc {
     uint64_t q, pool, page_table, seq_len, slots, out, workspace;
     int32_t batch, q_heads, kv_heads, head_dim, pages_per_seq, pages_per_split;
