@@ -377,7 +377,10 @@ lrm_status lrm_qwen_attention_ms(lrm_qwen q, float *ms);
  * from position len on. */
 lrm_status lrm_qwen_truncate(lrm_qwen q, int32_t slot, int32_t len);
 
-/* Replays the captured step `steps` times on the engine's stream (asynchronous; lrm_qwen_sync waits). */
+/* Replays the captured step `steps` times on the engine's stream (asynchronous; lrm_qwen_sync waits). The step's
+ * input ids are its rows' previous next ids, held in the engine's id buffer: after a prefill, or a decode call on
+ * other slots, the buffer holds other ids, and a replay is refused (LRM_ERR_STATE) until the graph's slots are
+ * decoded again or captured again with first ids. */
 lrm_status lrm_qwen_decode_replay(lrm_qwen q, int32_t steps);
 
 /* Device ids of the last replayed step (host copy, [batch]). */

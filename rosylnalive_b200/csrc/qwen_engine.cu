@@ -119,8 +119,13 @@ struct lrm_qwen_s {
     bool graph_timed = false;
     std::vector<cudaEvent_t> attn_ev;  // 2 per layer, recorded inside a timed graph
     std::vector<int32_t> graph_slots;
+    std::vector<int32_t> dev_slots;  // what d_slots holds (set_slots is its only writer): an unchanged list is not copied
+    // the slot list whose last step's next ids the id buffer holds (the input a replay of their graph reads); empty
+    // after a prefill, which fills the buffer with prompt ids
+    std::vector<int32_t> ids_slots;
     // staging
     uint32_t *h_pinned = nullptr;
+    uint32_t *h_err = nullptr;  // the error word read back on the stream, so one synchronise covers it
     int qkv_rows = 0;
 };
 
@@ -315,9 +320,10 @@ static lrm_status check_ready(lrm_qwen Q) {
 }
 
 static lrm_status sync_check(lrm_qwen Q) {
+    // the kernels write the error word on this stream: read it back behind them, then wait once
+    QTRY(Q, cudaMemcpyAsync(Q->h_err, Q->err, 4, cudaMemcpyDeviceToHost, Q->stream), "error word");
     QTRY(Q, cudaStreamSynchronize(Q->stream), "stream");
-    uint32_t code = 0;
-    QTRY(Q, cudaMemcpy(&code, Q->err, 4, cudaMemcpyDeviceToHost), "error word");
+    const uint32_t code = *Q->h_err;
     if (code) {
         cudaMemset(Q->err, 0, 4);
         char buf[96];
@@ -458,6 +464,7 @@ lrm_status lrm_qwen_create_stage(int32_t device, const lrm_qwen_config *cfg, int
     Q->ss = carve<float>(p, (size_t)(H / 128) * Q->ss_stride);
     if ((size_t)(p - Q->amem) > abytes) return qfail(Q.get(), LRM_ERR_STATE, "activation plan overflow");
     QTRY(Q.get(), cudaMallocHost(&Q->h_pinned, sizeof(uint32_t) * (size_t)T * 4), "pinned staging");
+    QTRY(Q.get(), cudaMallocHost(&Q->h_err, sizeof(uint32_t)), "pinned error word");
     *out = Q.release();
     return LRM_OK;
 }
@@ -476,6 +483,7 @@ lrm_status lrm_qwen_destroy(lrm_qwen Q) {
     cudaFree(Q->d_seq_len);
     cudaFree(Q->amem);
     cudaFreeHost(Q->h_pinned);
+    cudaFreeHost(Q->h_err);
     cudaStreamDestroy(Q->stream);
     delete Q;
     return LRM_OK;
@@ -721,7 +729,10 @@ static lrm_status run_prefill(lrm_qwen Q, int32_t nseq, const int32_t *slots, co
     std::vector<int32_t> new_len(nseq);
     for (int i = 0; i < nseq; ++i) new_len[i] = past[i] + lens[i];
     cudaStream_t st = Q->stream;
-    if (Q->is_first) QTRY(Q, cudaMemcpyAsync(Q->ids, ids, 4 * (size_t)T, cudaMemcpyHostToDevice, st), "ids");
+    if (Q->is_first) {
+        Q->ids_slots.clear();
+        QTRY(Q, cudaMemcpyAsync(Q->ids, ids, 4 * (size_t)T, cudaMemcpyHostToDevice, st), "ids");
+    }
     QTRY(Q, cudaMemcpyAsync(Q->tok_slot, tslot.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "slots");
     QTRY(Q, cudaMemcpyAsync(Q->tok_pos, tpos.data(), 4 * (size_t)T, cudaMemcpyHostToDevice, st), "positions");
     QTRY(Q, cudaMemcpyAsync(Q->cu, cu.data(), 4 * (size_t)(nseq + 1), cudaMemcpyHostToDevice, st), "cu_seqlens");
@@ -843,7 +854,11 @@ static lrm_status set_slots(lrm_qwen Q, int32_t batch, const int32_t *slots) {
         for (int b2 = 0; b2 < b; ++b2)
             if (slots[b2] == s) return qfail(Q, LRM_ERR_ARGUMENT, "a slot appears twice in one step");
     }
+    if ((int)Q->dev_slots.size() == batch && std::equal(Q->dev_slots.begin(), Q->dev_slots.end(), slots))
+        return LRM_OK;  // d_slots already holds this list (a greedy loop passes the same slots every step)
+    Q->dev_slots.clear();
     QTRY(Q, cudaMemcpyAsync(Q->d_slots, slots, 4 * (size_t)batch, cudaMemcpyHostToDevice, Q->stream), "slots");
+    Q->dev_slots.assign(slots, slots + batch);
     return LRM_OK;
 }
 
@@ -876,11 +891,16 @@ lrm_status lrm_qwen_decode(lrm_qwen Q, int32_t batch, const int32_t *slots, cons
     cudaGraphExec_t use_graph = nullptr;  // a kept capture of this exact slot list, if any
     for (const auto &k : Q->kept)
         if ((int)k.slots.size() == batch && std::equal(k.slots.begin(), k.slots.end(), slots)) use_graph = k.exec;
+    if (Q->is_first) Q->ids_slots.clear();
     if (use_graph) {
         QTRY(Q, cudaGraphLaunch(use_graph, st), "graph launch");
     } else {
         LTRY(decode_step(Q, batch));
+        // as the captured step does: the next ids become the id buffer's contents, the input of a later replay
+        if (Q->is_first && Q->is_last)
+            QTRY(Q, cudaMemcpyAsync(Q->ids, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToDevice, st), "feedback");
     }
+    if (Q->is_first && Q->is_last) Q->ids_slots.assign(slots, slots + batch);
     if (Q->is_last) {
         QTRY(Q, cudaMemcpyAsync(Q->h_pinned + batch, Q->next, 4 * (size_t)batch, cudaMemcpyDeviceToHost, st),
              "next");
@@ -906,6 +926,7 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
     if (first_ids) {
         memcpy(Q->h_pinned, first_ids, 4 * (size_t)batch);
         QTRY(Q, cudaMemcpyAsync(Q->ids, Q->h_pinned, 4 * (size_t)batch, cudaMemcpyHostToDevice, Q->stream), "ids");
+        Q->ids_slots.assign(slots, slots + batch);
     }
     LTRY(sync_check(Q));
     // a new capture replaces one of the same slot list, else the oldest once kKeptGraphs are kept
@@ -953,6 +974,13 @@ lrm_status lrm_qwen_decode_graph(lrm_qwen Q, int32_t batch, const int32_t *slots
 lrm_status lrm_qwen_decode_replay(lrm_qwen Q, int32_t steps) {
     LTRY(check_ready(Q));
     if (!Q->graph) return qfail(Q, LRM_ERR_STATE, "no decode graph captured");
+    // The graph's input ids are its rows' previous next ids in the id buffer; a prefill or a decode call on other
+    // slots since then has replaced them.
+    if (Q->is_first && Q->is_last && Q->ids_slots != Q->graph_slots)
+        return qfail(Q, LRM_ERR_STATE,
+                     "the id buffer holds another call's ids: capture again with first ids, or decode these slots");
+    // the graph reads its rows' slots from d_slots, which a decode call with another slot list may have replaced
+    LTRY(set_slots(Q, Q->graph_batch, Q->graph_slots.data()));
     LTRY(ensure_pages(Q, Q->graph_batch, Q->graph_slots.data(), steps));
     for (int i = 0; i < steps; ++i) QTRY(Q, cudaGraphLaunch(Q->graph, Q->stream), "graph launch");
     for (int b = 0; b < Q->graph_batch; ++b) Q->h_seq_len[Q->graph_slots[b]] += steps;

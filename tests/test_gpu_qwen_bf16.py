@@ -150,6 +150,36 @@ def test_graph_replay_equals_eager_decode(mini):
     assert eng.seq_len(0) == len(prompts[0]) + 6
 
 
+def test_replay_after_a_decode_of_other_slots(mini):
+    """A captured step reads its rows' slots and previous next ids from the engine's buffers. A decode call on other
+    slots replaces both, so a replay then is refused (not run on the other rows' ids); once the graph's own slots
+    are decoded again, replays continue exactly as eager decoding does."""
+    from rosylnalive_b200 import native as N
+
+    cfg, om, eng = mini
+    pa = [S.random_prompt(cfg.vocab, 12 + i, seed=60 + i, stream=f"ra{i}") for i in range(2)]
+    pb = [S.random_prompt(cfg.vocab, 15 + i, seed=70 + i, stream=f"rb{i}") for i in range(2)]
+    A, B = [4, 5], [6, 7]
+    cur, _ = eng.prefill(A, pa)
+    ref = [cur]
+    for _ in range(3):
+        cur, _ = eng.decode(A, cur)
+        ref.append(cur)
+    first_a, _ = eng.prefill(A, pa)
+    first_b, _ = eng.prefill(B, pb)
+    eng.capture(A, first_a)
+    eng.replay(1)
+    assert np.array_equal(eng.last_ids(), ref[1])
+    eng.decode(B, first_b)
+    with pytest.raises(N.GpuContractException):
+        eng.replay(1)
+    nxt, _ = eng.decode(A, ref[1])
+    assert np.array_equal(nxt, ref[2])
+    eng.replay(1)
+    assert np.array_equal(eng.last_ids(), ref[3])
+    assert eng.seq_len(4) == len(pa[0]) + 3
+
+
 def test_decode_batch_invariance(mini):
     """A sequence decoded alone and inside a batch gives the same tokens (fixed split shapes per length)."""
     cfg, om, eng = mini
