@@ -308,6 +308,10 @@ def run_ours(args, dist):
 
     ms_e2e = timed(e2e_steps)
     e2e_value = B * dist.world * K / (ms_e2e / 1000.0)
+    # Bytes the e2e steps copy: in, the B ids each step (the slot list is already on the device, and the pages of
+    # these positions were reserved by the replay above: truncate keeps them, so no page-table row is uploaded);
+    # out, the B next ids and the 4-byte error word.
+    e2e_h2d = 4 * B
 
     # Roofline of the dominant kernel (decode attention): events around each layer's launch inside the step.
     for s in slots:
@@ -356,7 +360,8 @@ def run_ours(args, dist):
                 "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
                 "config": decode_config(B, ctx, dist.world, cfg.layers),
-                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B},
+                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": e2e_h2d,
+                        "d2h_bytes_per_step": 4 * B + 4},
                 "gpu_launches": launches_per_step * K * dist.world, "roofline": roofline, "step_roofline": step_roof,
                 "prefill": prefill, "cpu_baseline": cpu, "clocks": clocks}
         print(json.dumps(line), flush=True)

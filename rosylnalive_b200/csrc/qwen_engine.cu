@@ -671,21 +671,28 @@ lrm_status lrm_qwen_reset_seq(lrm_qwen Q, int32_t slot) {
     return upload_page_row(Q, slot);
 }
 
-lrm_status lrm_qwen_reserve(lrm_qwen Q, int32_t slot, int32_t tokens) {
-    if (!Q || slot < 0 || slot >= Q->c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "slot out of range");
-    if (tokens > Q->c.max_pos) return qfail(Q, LRM_ERR_ARGUMENT, "tokens beyond max_pos");
-    cudaSetDevice(Q->device);
-    int need = (tokens + kPageTokens - 1) / kPageTokens;
+// Gives `slot` pages for `tokens` in the host copy of its page-table row; *changed says whether the row grew.
+static lrm_status reserve_host(lrm_qwen Q, int32_t slot, int32_t tokens, bool *changed) {
+    const int need = (tokens + kPageTokens - 1) / kPageTokens;
     auto &pg = Q->slot_pages[slot];
-    bool changed = false;
+    *changed = false;
     while ((int)pg.size() < need) {
         if (Q->free_pages.empty()) return qfail(Q, LRM_ERR_OUT_OF_MEMORY, "the KV pool has no free page");
         int32_t id = Q->free_pages.back();
         Q->free_pages.pop_back();
         Q->h_pages[(size_t)slot * Q->maxp + pg.size()] = id;
         pg.push_back(id);
-        changed = true;
+        *changed = true;
     }
+    return LRM_OK;
+}
+
+lrm_status lrm_qwen_reserve(lrm_qwen Q, int32_t slot, int32_t tokens) {
+    if (!Q || slot < 0 || slot >= Q->c.max_seqs) return qfail(Q, LRM_ERR_ARGUMENT, "slot out of range");
+    if (tokens > Q->c.max_pos) return qfail(Q, LRM_ERR_ARGUMENT, "tokens beyond max_pos");
+    cudaSetDevice(Q->device);
+    bool changed = false;
+    LTRY(reserve_host(Q, slot, tokens, &changed));
     return changed ? upload_page_row(Q, slot) : LRM_OK;
 }
 
@@ -862,14 +869,30 @@ static lrm_status set_slots(lrm_qwen Q, int32_t batch, const int32_t *slots) {
     return LRM_OK;
 }
 
-// Host-side checks before a step: every slot must have a page for its next position.
+// Host-side checks before a step: every slot must have a page for its next position. The rows that grew go to the
+// device table in one asynchronous copy per run of consecutive slots (sequences of equal length cross a page boundary
+// on the same step, and a per-row copy with a wait each stalled that step); the copy from pageable memory is staged
+// before it returns, and the step's own synchronise reports any error.
 static lrm_status ensure_pages(lrm_qwen Q, int32_t batch, const int32_t *slots, int steps) {
+    std::vector<int32_t> grown;
     for (int b = 0; b < batch; ++b) {
         const int s = slots[b];
         if (Q->h_seq_len[s] < 1) return qfail(Q, LRM_ERR_STATE, "decode needs a prefilled slot");
         const int need = Q->h_seq_len[s] + steps;
         if (need > Q->c.max_pos) return qfail(Q, LRM_ERR_ARGUMENT, "the sequence would pass max_pos");
-        LTRY(lrm_qwen_reserve(Q, s, need));
+        bool changed = false;
+        LTRY(reserve_host(Q, s, need, &changed));
+        if (changed) grown.push_back(s);
+    }
+    std::sort(grown.begin(), grown.end());
+    for (size_t i = 0; i < grown.size();) {
+        size_t j = i + 1;
+        while (j < grown.size() && grown[j] == grown[j - 1] + 1) ++j;
+        const size_t off = (size_t)grown[i] * Q->maxp, n = (j - i) * (size_t)Q->maxp;
+        QTRY(Q, cudaMemcpyAsync(Q->d_pages + off, &Q->h_pages[off], sizeof(int32_t) * n, cudaMemcpyHostToDevice,
+                                Q->stream),
+             "page table");
+        i = j;
     }
     return LRM_OK;
 }
