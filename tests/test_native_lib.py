@@ -5,6 +5,7 @@ import hashlib
 import os
 import re
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -97,3 +98,20 @@ def test_operators_refuse_sizes_past_their_int32_bound():
     assert N.lib().lrm_op_decode_gemm(None, ctypes.byref(d)) == N.LRM_ERR_ARGUMENT
     g = O.GemmDesc(m=128, n=128, k=(1 << 31) - 1, a=0x10000, b=0x10000, epilogue=O.GEMM_F32)
     assert N.lib().lrm_op_gemm_bf16(None, ctypes.byref(g)) == N.LRM_ERR_ARGUMENT
+
+
+def test_product_path_fails_loudly_without_the_library():
+    # No CPU fallback: with liblrmcuda.so absent, the first call into the product raises NativeLibraryMissing.
+    code = (
+        "import rosylnalive_b200.native as N\n"
+        "N.LIB_PATH = '/nonexistent/liblrmcuda.so'\n"
+        "from rosylnalive_b200 import ops, rope as R\n"
+        "for call in (lambda: R.t_spec(R.QWEN3_INV_FREQ_BITS, 16), lambda: ops.error_word()):\n"
+        "    try:\n"
+        "        call()\n"
+        "        print('RAN')\n"
+        "    except N.NativeLibraryMissing:\n"
+        "        print('MISSING')\n"
+    )
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert out.stdout.split() == ["MISSING", "MISSING"], out.stdout + out.stderr
